@@ -1,0 +1,116 @@
+"""ctypes binding of the C ABI in include/b2g_gemm.h.
+
+This is the same binding a non-Torch host would write (cgo / JNI / N-API
+stubs look alike): plain structs, pointers and sizes.  Device pointers and
+streams are passed as integers (e.g. `tensor.data_ptr()`,
+`torch.cuda.current_stream().cuda_stream`).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+from . import LIB_PATH
+
+B2G_OK = 0
+B2G_ERR_INVALID_ARG = 1
+B2G_ERR_UNSUPPORTED = 2
+B2G_ERR_WORKSPACE = 3
+B2G_ERR_LAUNCH = 4
+B2G_ERR_DEVICE_TIMEOUT = 5
+B2G_ERR_NO_DEVICE = 6
+
+OP_GEMM, OP_TRI_UPPER, OP_TRI_LOWER = 0, 1, 2
+PREC_TF32, PREC_3XTF32 = 0, 1
+
+
+class GemmDesc(C.Structure):
+    _fields_ = [
+        ("op", C.c_int32), ("precision", C.c_int32),
+        ("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64), ("batch", C.c_int64),
+        ("a", C.c_void_p), ("lda", C.c_int64), ("stride_a", C.c_int64), ("trans_a", C.c_int32),
+        ("b", C.c_void_p), ("ldb", C.c_int64), ("stride_b", C.c_int64), ("trans_b", C.c_int32),
+        ("c", C.c_void_p), ("ldc", C.c_int64), ("stride_c", C.c_int64),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_int64),
+    ]
+
+
+class GemmPlan(C.Structure):
+    _fields_ = [
+        ("block_m", C.c_int32), ("block_n", C.c_int32), ("block_k", C.c_int32),
+        ("stages", C.c_int32), ("tiles_m", C.c_int32), ("tiles_n", C.c_int32),
+        ("splits", C.c_int32), ("kb_per_split", C.c_int32), ("grid", C.c_int32),
+        ("stage_a", C.c_int32), ("stage_b", C.c_int32),
+        ("a_mn_major", C.c_int32), ("b_mn_major", C.c_int32),
+        ("work_units", C.c_int64), ("workspace_bytes", C.c_int64),
+    ]
+
+
+_lib = None
+
+
+def lib(path: Path | None = None) -> C.CDLL:
+    """Load libb2g_sm100.so (no GPU needed to load it or to plan)."""
+    global _lib
+    if _lib is None or path is not None:
+        h = C.CDLL(str(path or LIB_PATH))
+        h.b2g_gemm_plan_for.argtypes = [C.POINTER(GemmDesc), C.c_int, C.POINTER(GemmPlan)]
+        h.b2g_gemm_plan_for.restype = C.c_int
+        h.b2g_gemm_workspace_bytes.argtypes = [C.POINTER(GemmDesc)]
+        h.b2g_gemm_workspace_bytes.restype = C.c_int64
+        h.b2g_gemm.argtypes = [C.POINTER(GemmDesc), C.c_void_p]
+        h.b2g_gemm.restype = C.c_int
+        h.b2g_rowscale.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
+                                   C.c_int64, C.c_int64, C.c_void_p]
+        h.b2g_rowscale.restype = C.c_int
+        h.b2g_read_device_error.argtypes = [C.c_int, C.POINTER(C.c_int32)]
+        h.b2g_read_device_error.restype = C.c_int
+        h.b2g_status_string.argtypes = [C.c_int]
+        h.b2g_status_string.restype = C.c_char_p
+        h.b2g_version.argtypes = []
+        h.b2g_version.restype = C.c_int
+        if path is None:
+            _lib = h
+        return h
+    return _lib
+
+
+def make_desc(m, n, k, *, a=0, lda=None, b=0, ldb=None, c=0, ldc=None, batch=1, stride_a=0,
+              stride_b=0, stride_c=0, trans_a=0, trans_b=0, op=OP_GEMM, precision=PREC_TF32,
+              workspace=0, workspace_bytes=0) -> GemmDesc:
+    if lda is None:
+        lda = m if trans_a else k
+    if ldb is None:
+        ldb = k if trans_b else n
+    if ldc is None:
+        ldc = n
+    return GemmDesc(op, precision, m, n, k, batch, a, lda, stride_a, trans_a, b, ldb, stride_b,
+                    trans_b, c, ldc, stride_c, workspace, workspace_bytes)
+
+
+def plan(desc: GemmDesc, num_sms: int = 148) -> GemmPlan:
+    p = GemmPlan()
+    rc = lib().b2g_gemm_plan_for(C.byref(desc), num_sms, C.byref(p))
+    if rc != B2G_OK:
+        raise ValueError(f"b2g_gemm_plan_for: {status_string(rc)} ({rc})")
+    return p
+
+
+def gemm(desc: GemmDesc, stream: int = 0) -> int:
+    return lib().b2g_gemm(C.byref(desc), C.c_void_p(stream))
+
+
+def rowscale(d, b, out, rows, cols, ldb, ldo, stream: int = 0) -> int:
+    return lib().b2g_rowscale(d, b, out, rows, cols, ldb, ldo, C.c_void_p(stream))
+
+
+def read_device_error(device: int = 0) -> int:
+    code = C.c_int32(0)
+    rc = lib().b2g_read_device_error(device, C.byref(code))
+    if rc != B2G_OK:
+        raise RuntimeError(f"b2g_read_device_error: {status_string(rc)}")
+    return code.value
+
+
+def status_string(rc: int) -> str:
+    return lib().b2g_status_string(rc).decode()

@@ -1,0 +1,452 @@
+// b2g_capi.cu — host dispatcher and C ABI (include/b2g_gemm.h).
+//
+// The dispatcher is pure host arithmetic (b2g_gemm_plan_for): tile width,
+// pipeline depth, split-K and the persistent grid for a descriptor on a GPU
+// with a given SM count.  b2g_gemm() turns the plan into tensor maps and one
+// launch of the persistent tcgen05 engine; operands whose pitch or base
+// breaks TMA's 16-byte rule are first copied to an aligned pitch in the
+// caller's workspace.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/b2g_gemm.h"
+#include "gemm_engine.cuh"
+
+namespace b2g {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
+
+// ---------------------------------------------------------------- per-device state
+struct DeviceState {
+  bool init = false;
+  int num_sms = 0;
+  int* err_word = nullptr;      // device error word (4 bytes)
+};
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+
+int device_state(DeviceState** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B2G_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.init) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return B2G_ERR_NO_DEVICE;
+    if (prop.major != 10) return B2G_ERR_NO_DEVICE;
+    st.num_sms = prop.multiProcessorCount;
+    if (cudaMalloc(&st.err_word, sizeof(int)) != cudaSuccess) return B2G_ERR_LAUNCH;
+    if (cudaMemset(st.err_word, 0, sizeof(int)) != cudaSuccess) return B2G_ERR_LAUNCH;
+    st.init = true;
+  }
+  *out = &st;
+  return B2G_OK;
+}
+
+// ---------------------------------------------------------------- tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Rank-3 fp32 map {inner, outer, batch}.  K-major operands use the 128-byte
+// swizzle (16-byte chunks); MN-major operands the 128-byte swizzle with
+// 32-byte atoms, the shared-memory layout tcgen05 reads MN-major TF32 from.
+bool make_map(CUtensorMap* map, const float* base, int64_t inner, int64_t outer, int64_t batch,
+              int64_t ld, int64_t bstride, uint32_t box_inner, uint32_t box_outer, bool mn_major) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  if (batch <= 1) {
+    batch = 1;
+    bstride = round_up(ld * outer, 4);
+  }
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(bstride) * 4};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------- staging copy
+// dst[b][r][c] = src[b*sstride + r*sld + c], dst pitch dld (multiple of 4).
+__global__ void pitch_copy_kernel(const float* __restrict__ src, float* __restrict__ dst,
+                                  int64_t rows, int64_t cols, int64_t sld, int64_t sstride,
+                                  int64_t dld, int64_t dstride, int64_t batch) {
+  const int64_t total = batch * rows;
+  for (int64_t rr = blockIdx.x; rr < total; rr += gridDim.x) {
+    const int64_t b = rr / rows, r = rr - b * rows;
+    const float* s = src + b * sstride + r * sld;
+    float* d = dst + b * dstride + r * dld;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) d[c] = __ldg(s + c);
+  }
+}
+
+// ---------------------------------------------------------------- row scale
+// out[i][j] = d[i] * B[i][j]; 16-byte loads/stores when the layout allows.
+__global__ void __launch_bounds__(256) rowscale_vec_kernel(const float* __restrict__ d,
+                                                           const float4* __restrict__ b,
+                                                           float4* __restrict__ out,
+                                                           int64_t cols4, int64_t ldb4,
+                                                           int64_t ldo4) {
+  constexpr int kUnroll = 4;
+  const int64_t row = blockIdx.y;
+  const float s = __ldg(d + row);
+  const float4* src = b + row * ldb4;
+  float4* dst = out + row * ldo4;
+  int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x * kUnroll + threadIdx.x;
+  float4 v[kUnroll];
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t cc = c + static_cast<int64_t>(u) * blockDim.x;
+    if (cc < cols4) v[u] = __ldcs(src + cc);
+  }
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t cc = c + static_cast<int64_t>(u) * blockDim.x;
+    if (cc < cols4) {
+      float4 o;
+      o.x = v[u].x * s;
+      o.y = v[u].y * s;
+      o.z = v[u].z * s;
+      o.w = v[u].w * s;
+      __stcs(dst + cc, o);
+    }
+  }
+}
+
+__global__ void rowscale_scalar_kernel(const float* __restrict__ d, const float* __restrict__ b,
+                                       float* __restrict__ out, int64_t rows, int64_t cols,
+                                       int64_t ldb, int64_t ldo) {
+  const int64_t row = blockIdx.y;
+  if (row >= rows) return;
+  const float s = __ldg(d + row);
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < cols;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[row * ldo + c] = b[row * ldb + c] * s;
+}
+
+// ---------------------------------------------------------------- engine instantiations
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF>
+int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const EngineParams& p, int grid,
+                  cudaStream_t stream) {
+  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>;
+  auto kern = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, X3, XF>;
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::kSmemBytes) != cudaSuccess)
+      return B2G_ERR_LAUNCH;
+    configured_dev = dev;
+  }
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
+}
+
+template <int BN, int STAGES, bool X3, bool XF>
+int launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb,
+                  const EngineParams& p, int grid, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_engine<BN, STAGES, false, false, X3, XF>(ma, mb, p, grid, st);
+  if (!a_mn && b_mn) return launch_engine<BN, STAGES, false, true, X3, XF>(ma, mb, p, grid, st);
+  if (a_mn && !b_mn) return launch_engine<BN, STAGES, true, false, X3, XF>(ma, mb, p, grid, st);
+  return launch_engine<BN, STAGES, true, true, X3, XF>(ma, mb, p, grid, st);
+}
+
+bool valid_desc(const b2g_gemm_desc* d) {
+  if (!d) return false;
+  if (d->m < 0 || d->n < 0 || d->k < 0 || d->batch < 1) return false;
+  if (d->op < B2G_OP_GEMM || d->op > B2G_OP_TRI_LOWER) return false;
+  if (d->precision != B2G_PREC_TF32 && d->precision != B2G_PREC_3XTF32) return false;
+  if (d->m > INT32_MAX / 2 || d->n > INT32_MAX / 2 || d->k > INT32_MAX / 2) return false;
+  if (d->batch > 65535) return false;
+  if (d->op != B2G_OP_GEMM && (d->m != d->n || d->n != d->k)) return false;
+  const int64_t a_inner = d->trans_a ? d->m : d->k;
+  const int64_t b_inner = d->trans_b ? d->k : d->n;
+  if (d->m > 0 && d->n > 0 && d->k > 0) {
+    if (!d->a || !d->b) return false;
+    if (d->lda < std::max<int64_t>(1, a_inner) || d->ldb < std::max<int64_t>(1, b_inner))
+      return false;
+    if (d->stride_a < 0 || d->stride_b < 0) return false;
+  }
+  if (d->m > 0 && d->n > 0) {
+    if (!d->c || d->ldc < std::max<int64_t>(1, d->n) || d->stride_c < 0) return false;
+    if (d->batch > 1 && d->stride_c < d->m * d->ldc) return false;
+  }
+  return true;
+}
+
+bool tma_ok(const float* p, int64_t ld, int64_t stride, int64_t batch) {
+  if (reinterpret_cast<uintptr_t>(p) % 16) return false;
+  if (ld % 4) return false;
+  if (batch > 1 && stride != 0 && stride % 4) return false;
+  return true;
+}
+
+// Staged copy geometry of an operand (rows x cols per batch, aligned pitch).
+struct Stage {
+  int64_t rows, cols, pitch, bstride, nbatch, bytes;
+};
+Stage stage_geom(int64_t rows, int64_t cols, int64_t nbatch) {
+  Stage s;
+  s.rows = rows;
+  s.cols = cols;
+  s.pitch = round_up(std::max<int64_t>(cols, 1), 4);
+  s.bstride = s.pitch * rows;
+  s.nbatch = nbatch;
+  s.bytes = round_up(s.bstride * nbatch * 4, 256);
+  return s;
+}
+
+}  // namespace
+}  // namespace b2g
+
+using namespace b2g;
+
+extern "C" int b2g_version(void) { return 100; }
+
+extern "C" const char* b2g_status_string(int s) {
+  switch (s) {
+    case B2G_OK: return "ok";
+    case B2G_ERR_INVALID_ARG: return "invalid argument";
+    case B2G_ERR_UNSUPPORTED: return "unsupported layout or shape";
+    case B2G_ERR_WORKSPACE: return "workspace missing or too small";
+    case B2G_ERR_LAUNCH: return "CUDA launch or API failure";
+    case B2G_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case B2G_ERR_NO_DEVICE: return "no sm_100 device is current";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_plan* pl) {
+  if (!valid_desc(d) || !pl || num_sms <= 0) return B2G_ERR_INVALID_ARG;
+  std::memset(pl, 0, sizeof(*pl));
+  const bool x3 = d->precision == B2G_PREC_3XTF32;
+  const int64_t tiles_m = cdiv(d->m, kBlockM);
+  const int64_t kb_total = cdiv(d->k, kBlockK);
+  const int64_t batch = d->batch;
+  int bn;
+  if (x3) {
+    bn = 128;
+  } else {
+    const int64_t t256 = tiles_m * cdiv(d->n, 256) * batch;
+    const int64_t t128 = tiles_m * cdiv(d->n, 128) * batch;
+    bn = (t256 * 2 < num_sms && t128 > t256) ? 128 : 256;
+  }
+  pl->block_m = kBlockM;
+  pl->block_n = bn;
+  pl->block_k = kBlockK;
+  pl->stages = x3 ? 3 : (bn == 256 ? 4 : 6);
+  pl->tiles_m = static_cast<int32_t>(tiles_m);
+  pl->tiles_n = static_cast<int32_t>(cdiv(d->n, bn));
+  const int64_t tiles = tiles_m * pl->tiles_n * batch;
+  int64_t splits = 1;
+  if (d->op == B2G_OP_GEMM && tiles > 0 && tiles * 4 < num_sms * 3 && kb_total >= 8) {
+    splits = std::max<int64_t>(1, std::min<int64_t>(num_sms / tiles, kb_total / 4));
+  }
+  int64_t kbps = std::max<int64_t>(1, cdiv(kb_total, splits));
+  splits = std::max<int64_t>(1, cdiv(kb_total, kbps));
+  pl->splits = static_cast<int32_t>(splits);
+  pl->kb_per_split = static_cast<int32_t>(kbps);
+  pl->work_units = tiles * splits;
+  pl->grid = static_cast<int32_t>(std::min<int64_t>(pl->work_units, num_sms));
+  pl->a_mn_major = d->trans_a ? 1 : 0;
+  pl->b_mn_major = d->trans_b ? 0 : 1;
+  const int64_t sa_batch = (d->stride_a == 0) ? 1 : batch;
+  const int64_t sb_batch = (d->stride_b == 0) ? 1 : batch;
+  pl->stage_a = tma_ok(d->a, d->lda, d->stride_a, sa_batch) ? 0 : 1;
+  pl->stage_b = tma_ok(d->b, d->ldb, d->stride_b, sb_batch) ? 0 : 1;
+  int64_t ws = 0;
+  if (pl->stage_a)
+    ws += stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, sa_batch).bytes;
+  if (pl->stage_b)
+    ws += stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, sb_batch).bytes;
+  pl->workspace_bytes = ws;
+  return B2G_OK;
+}
+
+extern "C" int64_t b2g_gemm_workspace_bytes(const b2g_gemm_desc* d) {
+  b2g_gemm_plan pl;
+  if (b2g_gemm_plan_for(d, 148, &pl) != B2G_OK) return -1;
+  return pl.workspace_bytes;
+}
+
+extern "C" int b2g_gemm(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {
+  if (!valid_desc(d)) return B2G_ERR_INVALID_ARG;
+  if (d->m == 0 || d->n == 0) return B2G_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  DeviceState* ds = nullptr;
+  int rc = device_state(&ds);
+  if (rc != B2G_OK) return rc;
+  b2g_gemm_plan pl;
+  rc = b2g_gemm_plan_for(d, ds->num_sms, &pl);
+  if (rc != B2G_OK) return rc;
+  if (pl.workspace_bytes > 0 && (!d->workspace || d->workspace_bytes < pl.workspace_bytes))
+    return B2G_ERR_WORKSPACE;
+
+  const float* a = d->a;
+  const float* b = d->b;
+  int64_t lda = d->lda, ldb = d->ldb, sa = d->stride_a, sb = d->stride_b;
+  const int64_t a_batch = (d->stride_a == 0) ? 1 : d->batch;
+  const int64_t b_batch = (d->stride_b == 0) ? 1 : d->batch;
+  char* ws = static_cast<char*>(d->workspace);
+  if (d->k > 0 && pl.stage_a) {
+    Stage g = stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, a_batch);
+    float* dst = reinterpret_cast<float*>(ws);
+    const int64_t nrows = g.rows * g.nbatch;
+    pitch_copy_kernel<<<static_cast<int>(std::min<int64_t>(nrows, 65535)), 256, 0, stream>>>(
+        a, dst, g.rows, g.cols, lda, sa, g.pitch, g.bstride, g.nbatch);
+    a = dst;
+    lda = g.pitch;
+    sa = (a_batch > 1) ? g.bstride : 0;
+    ws += g.bytes;
+  }
+  if (d->k > 0 && pl.stage_b) {
+    Stage g = stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, b_batch);
+    float* dst = reinterpret_cast<float*>(ws);
+    const int64_t nrows = g.rows * g.nbatch;
+    pitch_copy_kernel<<<static_cast<int>(std::min<int64_t>(nrows, 65535)), 256, 0, stream>>>(
+        b, dst, g.rows, g.cols, ldb, sb, g.pitch, g.bstride, g.nbatch);
+    b = dst;
+    ldb = g.pitch;
+    sb = (b_batch > 1) ? g.bstride : 0;
+    ws += g.bytes;
+  }
+
+  EngineParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = static_cast<int>(d->m);
+  p.N = static_cast<int>(d->n);
+  p.K = static_cast<int>(d->k);
+  p.batch = static_cast<int>(d->batch);
+  p.block_n = pl.block_n;
+  p.tiles_m = pl.tiles_m;
+  p.tiles_n = pl.tiles_n;
+  p.splits = pl.splits;
+  p.kb_total = static_cast<int>(cdiv(d->k, kBlockK));
+  p.kb_per_split = pl.kb_per_split;
+  p.group_m = 8;
+  p.tri = d->op == B2G_OP_TRI_UPPER ? kTriUpper : (d->op == B2G_OP_TRI_LOWER ? kTriLower : kTriNone);
+  p.a_batched = a_batch > 1;
+  p.b_batched = b_batch > 1;
+  p.work_units = pl.work_units;
+  p.C = d->c;
+  p.ldc = d->ldc;
+  p.stride_c = d->stride_c;
+  p.atomic_out = pl.splits > 1;
+  p.vec_ok = (reinterpret_cast<uintptr_t>(d->c) % 16 == 0) && (d->ldc % 4 == 0) &&
+             (d->batch == 1 || d->stride_c % 4 == 0);
+  p.err = ds->err_word;
+
+  if (p.atomic_out) {
+    // Split-K accumulates into C: clear it first.
+    for (int64_t bi = 0; bi < d->batch; ++bi) {
+      cudaError_t e = cudaMemset2DAsync(d->c + bi * d->stride_c, d->ldc * 4, 0, d->n * 4, d->m,
+                                        stream);
+      if (e != cudaSuccess) return B2G_ERR_LAUNCH;
+    }
+  }
+
+  CUtensorMap ma, mb;
+  const int bn = pl.block_n;
+  const int64_t k_ext = std::max<int64_t>(d->k, 1);
+  bool ok;
+  if (!pl.a_mn_major)
+    ok = make_map(&ma, a, k_ext, d->m, a_batch, lda, sa, kBlockK, kBlockM, false);
+  else
+    ok = make_map(&ma, a, d->m, k_ext, a_batch, lda, sa, 32, kBlockK, true);
+  if (!ok) return B2G_ERR_UNSUPPORTED;
+  if (!pl.b_mn_major)
+    ok = make_map(&mb, b, k_ext, d->n, b_batch, ldb, sb, kBlockK, bn, false);
+  else
+    ok = make_map(&mb, b, d->n, k_ext, b_batch, ldb, sb, 32, kBlockK, true);
+  if (!ok) return B2G_ERR_UNSUPPORTED;
+
+  const bool a_mn = pl.a_mn_major, b_mn = pl.b_mn_major;
+  const bool x3 = d->precision == B2G_PREC_3XTF32;
+  const bool tri = p.tri != kTriNone;
+  if (x3) return launch_majors<128, 3, true, true>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
+  if (bn == 256) {
+    if (tri) return launch_majors<256, 4, false, true>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
+    return launch_majors<256, 4, false, false>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
+  }
+  if (tri) return launch_majors<128, 6, false, true>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
+  return launch_majors<128, 6, false, false>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
+}
+
+extern "C" int b2g_rowscale(const float* d, const float* b, float* out, int64_t rows, int64_t cols,
+                            int64_t ldb, int64_t ldo, b2g_stream_t stream_handle) {
+  if (rows < 0 || cols < 0) return B2G_ERR_INVALID_ARG;
+  if (rows == 0 || cols == 0) return B2G_OK;
+  if (!d || !b || !out || ldb < cols || ldo < cols) return B2G_ERR_INVALID_ARG;
+  if (rows > 65535 * 64) return B2G_ERR_UNSUPPORTED;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  const bool vec = (reinterpret_cast<uintptr_t>(b) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(out) % 16 == 0) && cols % 4 == 0 &&
+                   ldb % 4 == 0 && ldo % 4 == 0;
+  // Rows go on grid.y (limit 65535); larger row counts are issued in slabs.
+  for (int64_t r0 = 0; r0 < rows; r0 += 65535) {
+    const int64_t nr = std::min<int64_t>(65535, rows - r0);
+    if (vec) {
+      const int64_t cols4 = cols / 4;
+      dim3 grid(static_cast<unsigned>(cdiv(cols4, 256 * 4)), static_cast<unsigned>(nr));
+      rowscale_vec_kernel<<<grid, 256, 0, stream>>>(
+          d + r0, reinterpret_cast<const float4*>(b + r0 * ldb),
+          reinterpret_cast<float4*>(out + r0 * ldo), cols4, ldb / 4, ldo / 4);
+    } else {
+      dim3 grid(static_cast<unsigned>(std::min<int64_t>(cdiv(cols, 256), 64)),
+                static_cast<unsigned>(nr));
+      rowscale_scalar_kernel<<<grid, 256, 0, stream>>>(d + r0, b + r0 * ldb, out + r0 * ldo, nr,
+                                                       cols, ldb, ldo);
+    }
+    if (cudaGetLastError() != cudaSuccess) return B2G_ERR_LAUNCH;
+  }
+  return B2G_OK;
+}
+
+extern "C" int b2g_read_device_error(int device, int32_t* code) {
+  if (!code || device < 0 || device >= kMaxDevices) return B2G_ERR_INVALID_ARG;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (cudaSetDevice(device) != cudaSuccess) return B2G_ERR_NO_DEVICE;
+  DeviceState* ds = nullptr;
+  int rc = device_state(&ds);
+  if (rc == B2G_OK) {
+    int v = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess ||
+        cudaMemcpy(&v, ds->err_word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemset(ds->err_word, 0, sizeof(int)) != cudaSuccess)
+      rc = B2G_ERR_LAUNCH;
+    *code = v;
+  }
+  cudaSetDevice(prev);
+  return rc;
+}

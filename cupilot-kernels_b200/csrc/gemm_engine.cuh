@@ -1,0 +1,511 @@
+// gemm_engine.cuh — the persistent, warp-specialised sm_100a fp32-input GEMM.
+//
+// One CTA per SM walks a list of work units (output tile x K-split).  Roles:
+//   warp 0      TMA producer: 128B-swizzled A/B boxes into a STAGES-deep
+//               mbarrier ring (full[s] / empty[s]).
+//   warp 1      TMEM owner and MMA issuer: tcgen05.mma.kind::tf32 from the
+//               shared-memory descriptors into a double-buffered fp32
+//               accumulator in TMEM (tmem_full[b] / tmem_empty[b]).
+//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> a per-warp
+//               swizzled shared-memory transpose -> coalesced 16-byte global
+//               stores (or fp32 atomics for split-K), with the triangular
+//               output mask applied on the way out.
+//   warps 6..9  (XF variants only) operand transform between TMA and MMA:
+//               triangular input masking (C = triu(triu(A) triu(B)) semantics
+//               of kernels/14_Matmul_for_upper_triangular_matrices_best_kernel.cu:74-85)
+//               and the 3xTF32 hi/lo split (ready[s]).
+//
+// Operand majorness lives in the descriptors, so A (M x K or K x M) and
+// B (K x N or N x K) are consumed in place: no transpose pass.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "ptx_sm100.cuh"
+
+namespace b2g {
+
+constexpr int kBlockM = 128;
+constexpr int kBlockK = 32;              // fp32 elements in one 128-byte swizzle row
+constexpr int kSwRowBytes = 128;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s per wait, then give up
+
+enum : int { kTriNone = 0, kTriUpper = 1, kTriLower = 2 };
+
+// Device error codes (written to the per-device error word, first one wins).
+enum : int {
+  kErrWaitEmpty = 0x101,
+  kErrWaitFull = 0x102,
+  kErrWaitReady = 0x103,
+  kErrWaitTmemEmpty = 0x104,
+  kErrWaitTmemFull = 0x105,
+  kErrWaitXform = 0x106,
+};
+
+struct EngineParams {
+  int M, N, K, batch;
+  int block_n;
+  int tiles_m, tiles_n;
+  int splits, kb_total, kb_per_split;
+  int group_m;
+  int tri;
+  int a_batched, b_batched;
+  long long work_units;
+  float* C;
+  long long ldc, stride_c;
+  int atomic_out;
+  int vec_ok;
+  int* err;
+};
+
+struct WorkUnit {
+  int b, tm, tn, kb_lo, kb_hi;
+};
+
+// Map a linear work-unit index to (batch, tile, K range).  Tiles are
+// rasterised in groups of group_m tile-rows so CTAs that run together share
+// B columns in L2; split-K pieces of one tile are adjacent.  Triangular ops
+// clip the K range to the structurally non-zero band and give tiles that
+// lie wholly in the masked triangle an empty range.
+__host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long w) {
+  WorkUnit u;
+  const int split = static_cast<int>(w % p.splits);
+  const long long t = w / p.splits;
+  const long long per_batch = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  u.b = static_cast<int>(t / per_batch);
+  const long long r = t % per_batch;
+  const long long span = static_cast<long long>(p.group_m) * p.tiles_n;
+  const int grp = static_cast<int>(r / span);
+  const int first_m = grp * p.group_m;
+  const int rem_m = p.tiles_m - first_m;
+  const int gsz = rem_m < p.group_m ? rem_m : p.group_m;
+  const long long rr = r - static_cast<long long>(grp) * span;
+  u.tm = first_m + static_cast<int>(rr % gsz);
+  u.tn = static_cast<int>(rr / gsz);
+  int lo = split * p.kb_per_split;
+  int hi = lo + p.kb_per_split;
+  if (hi > p.kb_total) hi = p.kb_total;
+  if (p.tri != kTriNone) {
+    const long long m0 = static_cast<long long>(u.tm) * kBlockM;
+    const long long n0 = static_cast<long long>(u.tn) * p.block_n;
+    long long klo, khi;
+    if (p.tri == kTriUpper) {  // k in [i, j]
+      klo = m0;
+      khi = n0 + p.block_n;
+      if (n0 + p.block_n - 1 < m0) khi = klo;       // tile wholly below the diagonal
+    } else {                   // k in [j, i]
+      klo = n0;
+      khi = m0 + kBlockM;
+      if (n0 > m0 + kBlockM - 1) khi = klo;          // tile wholly above the diagonal
+    }
+    if (khi > p.K) khi = p.K;
+    int tlo = static_cast<int>(klo / kBlockK);
+    int thi = khi > klo ? static_cast<int>((khi + kBlockK - 1) / kBlockK) : tlo;
+    if (tlo > lo) lo = tlo;
+    if (thi < hi) hi = thi;
+  }
+  if (hi < lo) hi = lo;
+  u.kb_lo = lo;
+  u.kb_hi = hi;
+  return u;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF>
+struct EngineCfg {
+  static constexpr int kABytes = kBlockM * kBlockK * 4;
+  static constexpr int kBBytes = BN * kBlockK * 4;
+  static constexpr int kStageTx = kABytes + kBBytes;
+  static constexpr int kOperandBufs = X3 ? 2 : 1;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = STAGES * kABytes;
+  static constexpr int kOffALo = STAGES * (kABytes + kBBytes);
+  static constexpr int kOffBLo = kOffALo + STAGES * kABytes;
+  static constexpr int kOffEpi = STAGES * (kABytes + kBBytes) * kOperandBufs;
+  static constexpr int kEpiWarps = 4;
+  static constexpr int kEpiBytes = kEpiWarps * 32 * 32 * 4;
+  static constexpr int kOffBar = kOffEpi + kEpiBytes;
+  static constexpr int kNumBars = 3 * STAGES + 4;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kThreads = XF ? 320 : 192;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
+  static_assert(BN % 32 == 0 && BN <= 256, "BN");
+  static_assert(!X3 || XF, "the 3xTF32 split runs in the transform warps");
+};
+
+__device__ __forceinline__ void record_error(int* err, volatile int* abort, int code) {
+  atomicCAS(err, 0, code);
+  *abort = 1;
+}
+
+// Zero (mask) and/or split one operand tile in shared memory.
+// Tile layout as TMA wrote it:
+//   !MN: 128-byte swizzle; rows are M (or N) indices, each row holds 32 K
+//        values, 16-byte chunk c stored at c ^ (row % 8).
+//   MN : 32-byte-atom swizzle; groups of 32 M (or N) values, within a group
+//        rows are K indices, 32-byte chunk c stored at c ^ (row % 4).
+// mn0 / k0 are the global coordinates of the tile's first element.
+// rule: 0 none, 1 zero where k < mn, 2 zero where k > mn.
+template <bool MN, int EXT, bool SPLIT>
+__device__ __forceinline__ void transform_tile(float* tile, float* lo_tile, int mn0, int k0,
+                                               int rule, int xt) {
+  constexpr int kChunks = EXT * kBlockK / 4;   // 16-byte chunks in the tile
+  if (rule == 0 && !SPLIT) return;
+#pragma unroll 4
+  for (int c = xt; c < kChunks; c += 128) {
+    int mn_base, k_base, mn_step, k_step;
+    if (!MN) {
+      const int row = c >> 3;
+      const int logc = (c & 7) ^ (row & 7);
+      mn_base = mn0 + row;
+      k_base = k0 + logc * 4;
+      mn_step = 0;
+      k_step = 1;
+    } else {
+      const int g = c / (kBlockK * 8);
+      const int rem = c - g * (kBlockK * 8);
+      const int krow = rem >> 3;
+      const int phys = rem & 7;                              // 16-byte chunk in the row
+      const int logc = ((((phys >> 1) ^ (krow & 3))) << 1) | (phys & 1);
+      mn_base = mn0 + g * 32 + logc * 4;
+      k_base = k0 + krow;
+      mn_step = 1;
+      k_step = 0;
+    }
+    float4 v = reinterpret_cast<float4*>(tile)[c];
+    float e[4] = {v.x, v.y, v.z, v.w};
+    bool changed = false;
+    if (rule != 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int mn = mn_base + q * mn_step;
+        const int k = k_base + q * k_step;
+        const bool zero = (rule == 1) ? (k < mn) : (k > mn);
+        if (zero && e[q] != 0.0f) {
+          e[q] = 0.0f;
+          changed = true;
+        }
+      }
+    }
+    if (SPLIT) {
+      float h[4], l[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        // hi keeps the 10 explicit mantissa bits a TF32 operand carries;
+        // lo = x - hi is exact in fp32.
+        h[q] = __uint_as_float(__float_as_uint(e[q]) & 0xFFFFE000u);
+        l[q] = e[q] - h[q];
+      }
+      reinterpret_cast<float4*>(tile)[c] = make_float4(h[0], h[1], h[2], h[3]);
+      reinterpret_cast<float4*>(lo_tile)[c] = make_float4(l[0], l[1], l[2], l[3]);
+    } else if (changed) {
+      reinterpret_cast<float4*>(tile)[c] = make_float4(e[0], e[1], e[2], e[3]);
+    }
+  }
+}
+
+__device__ __forceinline__ void store4(const EngineParams& p, float* crow, int grow, int gcol,
+                                       float v0, float v1, float v2, float v3) {
+  float e[4] = {v0, v1, v2, v3};
+  if (p.tri == kTriUpper) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (gcol + q < grow) e[q] = 0.0f;
+  } else if (p.tri == kTriLower) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (gcol + q > grow) e[q] = 0.0f;
+  }
+  if (p.vec_ok && gcol + 3 < p.N) {
+    float4* dst = reinterpret_cast<float4*>(crow + gcol);
+    if (p.atomic_out)
+      atomicAdd(dst, make_float4(e[0], e[1], e[2], e[3]));
+    else
+      *dst = make_float4(e[0], e[1], e[2], e[3]);
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (gcol + q < p.N) {
+        if (p.atomic_out)
+          atomicAdd(crow + gcol + q, e[q]);
+        else
+          crow[gcol + q] = e[q];
+      }
+    }
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF>
+__global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kThreads, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a,
+                     const __grid_constant__ CUtensorMap map_b, const EngineParams p) {
+  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* ready = bars + 2 * STAGES;
+  uint64_t* tmem_full = bars + 3 * STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+      ptx::mbar_init(&ready[s], 4);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(&tmem_full[b], 1);
+      ptx::mbar_init(&tmem_empty[b], Cfg::kEpiWarps);
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&map_a);
+    ptx::prefetch_tmap(&map_b);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (long long w = blockIdx.x; w < p.work_units && ok; w += gridDim.x) {
+        const WorkUnit u = decode_unit(p, w);
+        const int m0 = u.tm * kBlockM;
+        const int n0 = u.tn * BN;
+        const int ab = p.a_batched ? u.b : 0;
+        const int bb = p.b_batched ? u.b : 0;
+        for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) {
+            record_error(p.err, abort_flag, kErrWaitEmpty);
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(&full[s], Cfg::kStageTx);
+          uint8_t* sa = smem + Cfg::kOffA + s * Cfg::kABytes;
+          uint8_t* sb = smem + Cfg::kOffB + s * Cfg::kBBytes;
+          const int k0 = kb * kBlockK;
+          if (!A_MN) {
+            ptx::tma_load_3d(sa, &map_a, &full[s], k0, m0, ab);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBlockM / 32; ++j)
+              ptx::tma_load_3d(sa + j * kBlockK * kSwRowBytes, &map_a, &full[s], m0 + 32 * j, k0,
+                               ab);
+          }
+          if (!B_MN) {
+            ptx::tma_load_3d(sb, &map_b, &full[s], k0, n0, bb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 32; ++j)
+              ptx::tma_load_3d(sb + j * kBlockK * kSwRowBytes, &map_b, &full[s], n0 + 32 * j, k0,
+                               bb);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::idesc_tf32(kBlockM, BN, A_MN, B_MN);
+      // Canonical layouts (byte offsets).  K-major (128-byte swizzle): rows
+      // 128 B apart, 8-row atoms 1024 B apart (SBO), LBO unused; a K=8 step
+      // advances 32 B inside the row.  MN-major (32-byte-atom swizzle):
+      // groups of 32 M/N values kBlockK*128 B apart (LBO), 4-row K atoms
+      // 512 B apart (SBO); a K=8 step advances 8 rows = 1024 B.
+      constexpr uint32_t a_lbo = A_MN ? kBlockK * kSwRowBytes : 16;
+      constexpr uint32_t b_lbo = B_MN ? kBlockK * kSwRowBytes : 16;
+      constexpr uint32_t a_sbo = A_MN ? 512 : 1024;
+      constexpr uint32_t b_sbo = B_MN ? 512 : 1024;
+      constexpr uint32_t a_lay = A_MN ? ptx::kLayoutSw128Base32 : ptx::kLayoutSw128;
+      constexpr uint32_t b_lay = B_MN ? ptx::kLayoutSw128Base32 : ptx::kLayoutSw128;
+      constexpr uint32_t a_kstep = A_MN ? 8 * kSwRowBytes : 8 * 4;   // bytes per K=8 step
+      constexpr uint32_t b_kstep = B_MN ? 8 * kSwRowBytes : 8 * 4;
+      uint32_t it = 0, tl = 0;
+      bool ok = true;
+      for (long long w = blockIdx.x; w < p.work_units && ok; w += gridDim.x) {
+        const WorkUnit u = decode_unit(p, w);
+        if (u.kb_lo >= u.kb_hi) continue;
+        const int buf = tl & 1;
+        const uint32_t uph = (tl >> 1) & 1;
+        if (!ptx::mbar_wait(&tmem_empty[buf], uph ^ 1, abort_flag, kWaitLimitNs)) {
+          record_error(p.err, abort_flag, kErrWaitTmemEmpty);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        uint32_t acc = 0;
+        for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          uint64_t* gate = XF ? &ready[s] : &full[s];
+          if (!ptx::mbar_wait(gate, ph, abort_flag, kWaitLimitNs)) {
+            record_error(p.err, abort_flag, XF ? kErrWaitReady : kErrWaitFull);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sa = ptx::smem_addr(smem + Cfg::kOffA + s * Cfg::kABytes);
+          const uint32_t sb = ptx::smem_addr(smem + Cfg::kOffB + s * Cfg::kBBytes);
+          const uint32_t sal = ptx::smem_addr(smem + Cfg::kOffALo + s * Cfg::kABytes);
+          const uint32_t sbl = ptx::smem_addr(smem + Cfg::kOffBLo + s * Cfg::kBBytes);
+#pragma unroll
+          for (int k8 = 0; k8 < kBlockK / 8; ++k8) {
+            const uint64_t da = ptx::smem_desc(sa + k8 * a_kstep, a_lbo, a_sbo, a_lay);
+            const uint64_t db = ptx::smem_desc(sb + k8 * b_kstep, b_lbo, b_sbo, b_lay);
+            ptx::mma_tf32(d_tmem, da, db, idesc, acc);
+            acc = 1;
+            if (X3) {
+              const uint64_t dal = ptx::smem_desc(sal + k8 * a_kstep, a_lbo, a_sbo, a_lay);
+              const uint64_t dbl = ptx::smem_desc(sbl + k8 * b_kstep, b_lbo, b_sbo, b_lay);
+              ptx::mma_tf32(d_tmem, da, dbl, idesc, 1);
+              ptx::mma_tf32(d_tmem, dal, db, idesc, 1);
+            }
+          }
+          ptx::mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        ptx::mma_commit(&tmem_full[buf]);
+        ++tl;
+      }
+    }
+  } else if (warp < 2 + Cfg::kEpiWarps) {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;                  // TMEM lane quadrant this warp may read
+    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffEpi) + (warp - 2) * 32 * 32;
+    uint32_t tl = 0;
+    for (long long w = blockIdx.x; w < p.work_units; w += gridDim.x) {
+      const WorkUnit u = decode_unit(p, w);
+      const int m0 = u.tm * kBlockM;
+      const int n0 = u.tn * BN;
+      const int row_base = m0 + quad * 32;
+      float* cb = p.C + static_cast<long long>(u.b) * p.stride_c;
+      if (u.kb_lo >= u.kb_hi) {
+        // Structurally zero tile (or K == 0): write zeros unless accumulating.
+        if (!p.atomic_out && row_base < p.M) {
+          for (int it = 0; it < 8 * (BN / 32); ++it) {
+            const int r_local = (it & 7) * 4 + (lane >> 3);
+            const int gcol = n0 + (it >> 3) * 32 + (lane & 7) * 4;
+            const int grow = row_base + r_local;
+            if (grow < p.M && gcol < p.N)
+              store4(p, cb + static_cast<long long>(grow) * p.ldc, grow, gcol, 0.f, 0.f, 0.f, 0.f);
+          }
+        }
+        continue;
+      }
+      const int buf = tl & 1;
+      const uint32_t uph = (tl >> 1) & 1;
+      if (!ptx::mbar_wait(&tmem_full[buf], uph, abort_flag, kWaitLimitNs)) {
+        if (lane == 0) record_error(p.err, abort_flag, kErrWaitTmemFull);
+        break;
+      }
+      ptx::tc_fence_after();
+      if (row_base < p.M) {
+#pragma unroll 1
+        for (int ch = 0; ch < BN / 32; ++ch) {
+          const int col0 = n0 + ch * 32;
+          if (col0 >= p.N) break;
+          uint32_t r[32];
+          ptx::tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                      buf * BN + ch * 32,
+                                  r);
+          ptx::tmem_ld_wait();
+          // Row `lane` of this warp's 32x32 block -> swizzled staging row.
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4* dst = reinterpret_cast<float4*>(stg + lane * 32 + ((j ^ (lane & 7)) * 4));
+            *dst = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          }
+          __syncwarp();
+          // 8 lanes cover one 128-byte row segment: coalesced stores.
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int r_local = it * 4 + (lane >> 3);
+            const int jj = lane & 7;
+            const float4 v =
+                *reinterpret_cast<const float4*>(stg + r_local * 32 + ((jj ^ (r_local & 7)) * 4));
+            const int grow = row_base + r_local;
+            const int gcol = col0 + jj * 4;
+            if (grow < p.M && gcol < p.N)
+              store4(p, cb + static_cast<long long>(grow) * p.ldc, grow, gcol, v.x, v.y, v.z, v.w);
+          }
+          __syncwarp();
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&tmem_empty[buf]);
+      ++tl;
+    }
+  } else if (XF) {
+    // ------------------------------------------------------------ transform
+    const int xt = threadIdx.x - (2 + Cfg::kEpiWarps) * 32;
+    uint32_t it = 0;
+    bool ok = true;
+    for (long long w = blockIdx.x; w < p.work_units && ok; w += gridDim.x) {
+      const WorkUnit u = decode_unit(p, w);
+      const int m0 = u.tm * kBlockM;
+      const int n0 = u.tn * BN;
+      for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!ptx::mbar_wait(&full[s], ph, abort_flag, kWaitLimitNs)) {
+          if (lane == 0) record_error(p.err, abort_flag, kErrWaitXform);
+          ok = false;
+          break;
+        }
+        const int k0 = kb * kBlockK;
+        int rule_a = 0, rule_b = 0;
+        if (p.tri == kTriUpper) {          // A: zero k < i ; B: zero k > j
+          if (k0 < m0 + kBlockM - 1) rule_a = 1;
+          if (k0 + kBlockK - 1 > n0) rule_b = 2;
+        } else if (p.tri == kTriLower) {   // A: zero k > i ; B: zero k < j
+          if (k0 + kBlockK - 1 > m0) rule_a = 2;
+          if (k0 < n0 + BN - 1) rule_b = 1;
+        }
+        float* ta = reinterpret_cast<float*>(smem + Cfg::kOffA + s * Cfg::kABytes);
+        float* tb = reinterpret_cast<float*>(smem + Cfg::kOffB + s * Cfg::kBBytes);
+        float* tal = reinterpret_cast<float*>(smem + Cfg::kOffALo + s * Cfg::kABytes);
+        float* tbl = reinterpret_cast<float*>(smem + Cfg::kOffBLo + s * Cfg::kBBytes);
+        transform_tile<A_MN, kBlockM, X3>(ta, tal, m0, k0, rule_a, xt);
+        transform_tile<B_MN, BN, X3>(tb, tbl, n0, k0, rule_b, xt);
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&ready[s]);
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace b2g

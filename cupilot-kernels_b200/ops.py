@@ -1,0 +1,126 @@
+"""Per-operator entry points mirroring the reference's Part-3 host functions.
+
+The reference builds one JIT module per kernel file, each exporting a single
+`torch::Tensor <name>(torch::Tensor A, torch::Tensor B)`.  Here every
+operator is an object with `forward(A, B)` and an attribute carrying the
+reference's own function name, so both call styles drop in:
+
+    from cupilot_kernels_b200 import ops          # (package dir: cupilot-kernels_b200)
+    C = ops.p16.forward(A, B)                      # C = A^T B
+    C = ops.p16.matmul_transposed_cuda(A, B)       # same function
+
+Inputs: CUDA float32 tensors (A, B as the reference takes them).  Output:
+a new float32 tensor on the same device, produced on the current stream.
+Errors raise RuntimeError from TORCH_CHECK, as the reference's TORCH_CHECKs do.
+
+Precision: TF32 by default (`set_precision("3xtf32")` or the
+`precision("3xtf32")` context manager selects the split 3xTF32 mode).
+"""
+from __future__ import annotations
+
+import contextlib
+import os
+from dataclasses import dataclass
+from typing import Callable
+
+from . import native
+
+_ext = native()
+
+PRECISIONS = {"tf32": 0, "3xtf32": 1}
+
+
+def set_precision(mode: str) -> None:
+    """Select 'tf32' (one TF32 product) or '3xtf32' (split, ~fp32 accuracy)."""
+    if mode not in PRECISIONS:
+        raise ValueError(f"precision must be one of {sorted(PRECISIONS)}, got {mode!r}")
+    _ext.set_precision(PRECISIONS[mode])
+
+
+def get_precision() -> str:
+    v = _ext.get_precision()
+    return next(k for k, i in PRECISIONS.items() if i == v)
+
+
+@contextlib.contextmanager
+def precision(mode: str):
+    prev = get_precision()
+    set_precision(mode)
+    try:
+        yield
+    finally:
+        set_precision(prev)
+
+
+if os.environ.get("B2G_PRECISION"):
+    set_precision(os.environ["B2G_PRECISION"].lower())
+
+
+@dataclass(frozen=True)
+class Operator:
+    pid: int
+    name: str
+    ref_name: str           # the reference's Part-3 function name
+    ref_site: str           # reference file:line of that function
+    forward: Callable
+
+    def __call__(self, A, B):
+        return self.forward(A, B)
+
+    def __getattr__(self, item):
+        if item == self.ref_name:
+            return self.forward
+        raise AttributeError(item)
+
+
+_K = "kernels/"
+OPERATORS = {
+    1: Operator(1, "square", "matmul_cuda",
+                _K + "1_Square_matrix_multiplication_best_kernel.cu:189", _ext.square_matmul),
+    2: Operator(2, "standard", "matmul_cuda",
+                _K + "2_Standard_matrix_multiplication_best_kernel.cu:117", _ext.standard_matmul),
+    3: Operator(3, "batched", "batched_matmul_cuda",
+                _K + "3_Batched_matrix_multiplication_best_kernel.cu:113", _ext.batched_matmul),
+    6: Operator(6, "large_k", "matmul_cuda",
+                _K + "6_Matmul_with_large_K_dimension_best_kernel.cu:128", _ext.large_k_matmul),
+    7: Operator(7, "small_k", "gemm_cuda",
+                _K + "7_Matmul_with_small_K_dimension_best_kernel.cu:80", _ext.small_k_matmul),
+    8: Operator(8, "irregular", "matmul_cuda",
+                _K + "8_Matmul_with_irregular_shapes_best_kernel.cu:155", _ext.irregular_matmul),
+    9: Operator(9, "tall_skinny", "tall_skinny_matmul_cuda",
+                _K + "9_Tall_skinny_matrix_multiplication_best_kernel.cu:145",
+                _ext.tall_skinny_matmul),
+    10: Operator(10, "tensor3d", "batched_matmul_cuda",
+                 _K + "10_3D_tensor_matrix_multiplication_best_kernel.cu:180",
+                 _ext.tensor3d_matmul),
+    11: Operator(11, "tensor4d", "tensor_matmul_cuda",
+                 _K + "11_4D_tensor_matrix_multiplication_best_kernel.cu:132",
+                 _ext.tensor4d_matmul),
+    12: Operator(12, "diag", "diag_mult_cuda",
+                 _K + "12_Matmul_with_diagonal_matrices_best_kernel.cu:43", _ext.diag_matmul),
+    13: Operator(13, "symmetric", "symmetric_matmul_cuda",
+                 _K + "13_Matmul_for_symmetric_matrices_best_kernel.cu:134",
+                 _ext.symmetric_matmul),
+    14: Operator(14, "upper_tri", "upper_tri_matmul_cuda",
+                 _K + "14_Matmul_for_upper_triangular_matrices_best_kernel.cu:135",
+                 _ext.upper_tri_matmul),
+    15: Operator(15, "lower_tri", "lower_tri_mul_cuda",
+                 _K + "15_Matmul_for_lower_triangular_matrices_best_kernel.cu:155",
+                 _ext.lower_tri_matmul),
+    16: Operator(16, "transposed_a", "matmul_transposed_cuda",
+                 _K + "16_Matmul_with_transposed_A_best_kernel.cu:124",
+                 _ext.matmul_transposed_a),
+    17: Operator(17, "transposed_b", "matmul_cuda",
+                 _K + "17_Matmul_with_transposed_B_best_kernel.cu:267",
+                 _ext.matmul_transposed_b),
+    18: Operator(18, "transposed_both", "matmul_transposed_cuda",
+                 _K + "18_Matmul_with_transposed_both_best_kernel.cu:152",
+                 _ext.matmul_transposed_both),
+}
+
+for _pid, _op in OPERATORS.items():
+    globals()[f"p{_pid}"] = _op
+    globals()[_op.name] = _op
+
+gemm = _ext.gemm
+read_device_error = _ext.read_device_error

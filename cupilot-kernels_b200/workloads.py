@@ -1,0 +1,164 @@
+"""The benchmark configurations of the GEMM family, with seeded inputs.
+
+Each workload names one operator (reference problem ID), its shapes, the
+algorithmic work per call (2*M*N*K flops times batch; minimum fp32 bytes
+with each operand read once and the output written once) and the bound
+that work implies on B200.  Inputs are i.i.d. N(0, 1) fp32 drawn from a
+CPU `torch.Generator` seeded per workload, so host copies and device copies
+are bit-identical; structured operands follow the configs' recipes
+(opposite triangle zeroed; symmetric = (X + X^T) / 2).
+
+The shapes are the ones the benchmark configs state; the reference's own
+problem definitions are not available, so these stand in for them.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable, Dict, Tuple
+
+import torch
+
+
+@dataclass(frozen=True)
+class Workload:
+    name: str
+    pid: int
+    shapes: Dict[str, int]
+    seed: int
+    make: Callable[..., Tuple[torch.Tensor, torch.Tensor]] = field(repr=False)
+    flops: float
+    min_bytes: float
+    bound: str                 # "tensor" | "hbm"
+    useful_flops: float = 0.0  # triangular ops: flops of the non-zero band
+
+    def inputs(self, device="cpu", **override):
+        shapes = dict(self.shapes)
+        shapes.update(override)
+        g = torch.Generator().manual_seed(self.seed)
+        A, B = self.make(g, **shapes)
+        if device != "cpu":
+            A, B = A.to(device), B.to(device)
+        return A, B
+
+
+def _randn(g, *shape):
+    return torch.randn(*shape, generator=g, dtype=torch.float32)
+
+
+def _mk_nn(g, m, n, k):
+    return _randn(g, m, k), _randn(g, k, n)
+
+
+def _mk_tn(g, m, n, k):      # A stored (K, M)
+    return _randn(g, k, m), _randn(g, k, n)
+
+
+def _mk_nt(g, m, n, k):      # B stored (N, K)
+    return _randn(g, m, k), _randn(g, n, k)
+
+
+def _mk_tt(g, m, n, k):
+    return _randn(g, k, m), _randn(g, n, k)
+
+
+def _mk_bmm(g, batch, m, n, k):
+    return _randn(g, batch, m, k), _randn(g, batch, k, n)
+
+
+def _mk_3d(g, batch, m, n, k):
+    return _randn(g, batch, m, k), _randn(g, k, n)
+
+
+def _mk_4d(g, b, i, j, l, k):
+    return _randn(g, b, i, j, l), _randn(g, l, k)
+
+
+def _mk_diag(g, n):
+    return _randn(g, n), _randn(g, n, n)
+
+
+def _mk_upper(g, n):
+    return torch.triu(_randn(g, n, n)), torch.triu(_randn(g, n, n))
+
+
+def _mk_lower(g, n):
+    return torch.tril(_randn(g, n, n)), torch.tril(_randn(g, n, n))
+
+
+def _mk_sym(g, n):
+    X = _randn(g, n, n)
+    Y = _randn(g, n, n)
+    return (X + X.T) / 2, (Y + Y.T) / 2
+
+
+def _gemm_cost(m, n, k, batch=1, a_shared=False, b_shared=False):
+    flops = 2.0 * m * n * k * batch
+    a = m * k * (1 if a_shared else batch)
+    b = k * n * (1 if b_shared else batch)
+    c = m * n * batch
+    return flops, 4.0 * (a + b + c)
+
+
+def _tri_useful(n):
+    return 2.0 * n * (n + 1) * (n + 2) / 6.0
+
+
+def _w(name, pid, shapes, seed, make, cost, bound, useful=0.0):
+    flops, nbytes = cost
+    return Workload(name, pid, shapes, seed, make, flops, nbytes, bound, useful)
+
+
+WORKLOADS: Dict[str, Workload] = {}
+
+
+def _add(w: Workload):
+    WORKLOADS[w.name] = w
+
+
+# square
+_add(_w("square", 1, dict(m=2048, n=2048, k=2048), 0, _mk_nn, _gemm_cost(2048, 2048, 2048), "tensor"))
+# transposed operands, M=1024, K=4096, N=2048
+_add(_w("transposed_a", 16, dict(m=1024, n=2048, k=4096), 1, _mk_tn, _gemm_cost(1024, 2048, 4096), "tensor"))
+_add(_w("transposed_b", 17, dict(m=1024, n=2048, k=4096), 2, _mk_nt, _gemm_cost(1024, 2048, 4096), "tensor"))
+_add(_w("transposed_both", 18, dict(m=1024, n=2048, k=4096), 3, _mk_tt, _gemm_cost(1024, 2048, 4096), "tensor"))
+# batched and 3-D
+_add(_w("batched", 3, dict(batch=128, m=512, n=2048, k=1024), 4, _mk_bmm,
+        _gemm_cost(512, 2048, 1024, 128), "tensor"))
+_add(_w("tensor3d", 10, dict(batch=16, m=1024, n=768, k=2048), 5, _mk_3d,
+        _gemm_cost(16 * 1024, 768, 2048), "tensor"))
+# skewed shapes
+_add(_w("small_k", 7, dict(m=16384, n=16384, k=32), 6, _mk_nn, _gemm_cost(16384, 16384, 32), "hbm"))
+_add(_w("large_k", 6, dict(m=256, n=256, k=262144), 7, _mk_nn, _gemm_cost(256, 256, 262144), "hbm"))
+_add(_w("tall_skinny", 9, dict(m=16384, n=16384, k=64), 8, _mk_nn, _gemm_cost(16384, 16384, 64), "hbm"))
+_add(_w("irregular", 8, dict(m=8205, n=5921, k=2949), 9, _mk_nn, _gemm_cost(8205, 5921, 2949), "tensor"))
+# structured operands at N=4096, and the 4-D product
+_add(Workload("diag", 12, dict(n=4096), 10, _mk_diag, 4096.0 * 4096,
+              4.0 * (4096 + 2 * 4096 * 4096), "hbm"))
+_add(_w("upper_tri", 14, dict(n=4096), 11, _mk_upper, _gemm_cost(4096, 4096, 4096), "tensor",
+        _tri_useful(4096)))
+_add(_w("lower_tri", 15, dict(n=4096), 12, _mk_lower, _gemm_cost(4096, 4096, 4096), "tensor",
+        _tri_useful(4096)))
+_add(_w("symmetric", 13, dict(n=4096), 13, _mk_sym, _gemm_cost(4096, 4096, 4096), "tensor"))
+_add(_w("tensor4d", 11, dict(b=16, i=256, j=512, l=256, k=768), 14, _mk_4d,
+        _gemm_cost(16 * 256 * 512, 768, 256), "hbm"))
+
+
+def cost_for(name: str, **shapes) -> Tuple[float, float]:
+    """(flops, min_bytes) of a workload at overridden shapes."""
+    w = WORKLOADS[name]
+    s = dict(w.shapes)
+    s.update(shapes)
+    if name in ("square", "transposed_a", "transposed_b", "transposed_b", "transposed_both",
+                "small_k", "large_k", "tall_skinny", "irregular"):
+        return _gemm_cost(s["m"], s["n"], s["k"])
+    if name == "batched":
+        return _gemm_cost(s["m"], s["n"], s["k"], s["batch"])
+    if name == "tensor3d":
+        return _gemm_cost(s["batch"] * s["m"], s["n"], s["k"])
+    if name == "tensor4d":
+        return _gemm_cost(s["b"] * s["i"] * s["j"], s["k"], s["l"])
+    if name == "diag":
+        n = s["n"]
+        return float(n * n), 4.0 * (n + 2 * n * n)
+    n = s["n"]
+    return _gemm_cost(n, n, n)

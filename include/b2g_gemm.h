@@ -1,0 +1,141 @@
+/*
+ * b2g_gemm.h — C ABI of the B200 (sm_100a) fp32-input GEMM operator family.
+ *
+ * Plain pointers and sizes only; no torch types cross this boundary.  The
+ * Torch C++ binding (cupilot-kernels_b200/csrc/torch_binding.cpp) and any
+ * other host (ctypes, cgo, JNI) bind these symbols.
+ *
+ * The reference (champloo2878/cuPilot-Kernels) exposes one Part-3 host
+ * function per operator, each `torch::Tensor f(torch::Tensor A, torch::Tensor B)`
+ * launching a hand-written kernel.  Every one of those GEMM-band functions is
+ * replaced by b2g_gemm() with a descriptor that states the operator, the
+ * operand majorness and the triangle; diag_mult_cuda is replaced by
+ * b2g_rowscale():
+ *
+ *   kernels/1_Square_matrix_multiplication_best_kernel.cu:189   matmul_cuda              -> b2g_gemm (NN)
+ *   kernels/2_Standard_matrix_multiplication_best_kernel.cu:117 matmul_cuda              -> b2g_gemm (NN)
+ *   kernels/3_Batched_matrix_multiplication_best_kernel.cu:113  batched_matmul_cuda      -> b2g_gemm (NN, batch)
+ *   kernels/6_Matmul_with_large_K_dimension_best_kernel.cu:128  matmul_cuda              -> b2g_gemm (NN, split-K)
+ *   kernels/7_Matmul_with_small_K_dimension_best_kernel.cu:80   gemm_cuda                -> b2g_gemm (NN)
+ *   kernels/8_Matmul_with_irregular_shapes_best_kernel.cu:155   matmul_cuda              -> b2g_gemm (NN, staged)
+ *   kernels/9_Tall_skinny_matrix_multiplication_best_kernel.cu:145 tall_skinny_matmul_cuda -> b2g_gemm (NN)
+ *   kernels/10_3D_tensor_matrix_multiplication_best_kernel.cu:180 batched_matmul_cuda    -> b2g_gemm (NN, flattened)
+ *   kernels/11_4D_tensor_matrix_multiplication_best_kernel.cu:132 tensor_matmul_cuda     -> b2g_gemm (NN, flattened)
+ *   kernels/12_Matmul_with_diagonal_matrices_best_kernel.cu:43  diag_mult_cuda           -> b2g_rowscale
+ *   kernels/13_Matmul_for_symmetric_matrices_best_kernel.cu:134 symmetric_matmul_cuda    -> b2g_gemm (NT)
+ *   kernels/14_Matmul_for_upper_triangular_matrices_best_kernel.cu:135 upper_tri_matmul_cuda -> b2g_gemm (TRI_UPPER)
+ *   kernels/15_Matmul_for_lower_triangular_matrices_best_kernel.cu:155 lower_tri_mul_cuda -> b2g_gemm (TRI_LOWER)
+ *   kernels/16_Matmul_with_transposed_A_best_kernel.cu:124      matmul_transposed_cuda   -> b2g_gemm (TN)
+ *   kernels/17_Matmul_with_transposed_B_best_kernel.cu:267      matmul_cuda              -> b2g_gemm (NT)
+ *   kernels/18_Matmul_with_transposed_both_best_kernel.cu:152   matmul_transposed_cuda   -> b2g_gemm (TT)
+ *
+ * Error behaviour: every entry point returns a b2g_status; 0 is success.
+ * Nothing traps or asserts on the device.  Kernel-side waits are bounded;
+ * a wait that gives up writes a code into the per-device error word, which
+ * b2g_read_device_error() returns (and clears).
+ */
+#ifndef B2G_GEMM_H
+#define B2G_GEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2G_API __attribute__((visibility("default")))
+#else
+#define B2G_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Opaque stream handle: a cudaStream_t (CUstream) passed through as void*. */
+typedef void* b2g_stream_t;
+
+typedef enum b2g_status {
+  B2G_OK = 0,
+  B2G_ERR_INVALID_ARG = 1,      /* null pointer, negative size, bad enum   */
+  B2G_ERR_UNSUPPORTED = 2,      /* layout/shape the engine cannot express  */
+  B2G_ERR_WORKSPACE = 3,        /* workspace missing or too small          */
+  B2G_ERR_LAUNCH = 4,           /* CUDA launch / API call failed           */
+  B2G_ERR_DEVICE_TIMEOUT = 5,   /* a bounded device-side wait gave up      */
+  B2G_ERR_NO_DEVICE = 6         /* no sm_100 device current                */
+} b2g_status;
+
+typedef enum b2g_op {
+  B2G_OP_GEMM = 0,              /* C = op(A) . op(B)                       */
+  B2G_OP_TRI_UPPER = 1,         /* C = triu(triu(A) . triu(B)), square     */
+  B2G_OP_TRI_LOWER = 2          /* C = tril(tril(A) . tril(B)), square     */
+} b2g_op;
+
+typedef enum b2g_precision {
+  B2G_PREC_TF32 = 0,            /* one TF32 product per term               */
+  B2G_PREC_3XTF32 = 1           /* hi.hi + hi.lo + lo.hi split products    */
+} b2g_precision;
+
+/*
+ * One (optionally batched) GEMM, all fp32, C row-major:
+ *   C[b][m][n] = sum_k opA(A)[b][m][k] * opB(B)[b][k][n]
+ * trans_a == 0: A[b][m][k] at a[b*stride_a + m*lda + k]   (A stored M x K)
+ * trans_a == 1: A[b][m][k] at a[b*stride_a + k*lda + m]   (A stored K x M)
+ * trans_b == 0: B[b][k][n] at b[b*stride_b + k*ldb + n]   (B stored K x N)
+ * trans_b == 1: B[b][k][n] at b[b*stride_b + n*ldb + k]   (B stored N x K)
+ * stride_a / stride_b may be 0 (operand shared across the batch).
+ * All leading dimensions and strides are in elements.
+ */
+typedef struct b2g_gemm_desc {
+  int32_t op;                   /* b2g_op                                  */
+  int32_t precision;            /* b2g_precision                           */
+  int64_t m, n, k, batch;
+  const float* a; int64_t lda; int64_t stride_a; int32_t trans_a;
+  const float* b; int64_t ldb; int64_t stride_b; int32_t trans_b;
+  float* c;       int64_t ldc; int64_t stride_c;
+  void* workspace;              /* device memory, >= b2g_gemm_workspace_bytes() */
+  int64_t workspace_bytes;
+} b2g_gemm_desc;
+
+/* What the host dispatcher chose for a descriptor (pure host computation). */
+typedef struct b2g_gemm_plan {
+  int32_t block_m, block_n, block_k;
+  int32_t stages;
+  int32_t tiles_m, tiles_n;
+  int32_t splits;               /* split-K factor; >1 accumulates into a zeroed C */
+  int32_t kb_per_split;         /* K blocks of block_k per split           */
+  int32_t grid;                 /* persistent CTAs launched                */
+  int32_t stage_a, stage_b;     /* 1: operand copied to a 16-byte-aligned pitch in workspace */
+  int32_t a_mn_major, b_mn_major;
+  int64_t work_units;
+  int64_t workspace_bytes;
+} b2g_gemm_plan;
+
+/* Compute the plan for desc on a GPU with num_sms SMs (no device access). */
+B2G_API int b2g_gemm_plan_for(const b2g_gemm_desc* desc, int num_sms, b2g_gemm_plan* plan);
+
+/* Workspace the caller must provide for desc (0 for aligned layouts). */
+B2G_API int64_t b2g_gemm_workspace_bytes(const b2g_gemm_desc* desc);
+
+/* Launch the GEMM on stream (asynchronous; no host synchronisation). */
+B2G_API int b2g_gemm(const b2g_gemm_desc* desc, b2g_stream_t stream);
+
+/*
+ * out[i][j] = d[i] * B[i][j]   — diag(d) . B, one rounding per element.
+ * Replaces diag_mult_cuda (kernels/12_Matmul_with_diagonal_matrices_best_kernel.cu:43).
+ */
+B2G_API int b2g_rowscale(const float* d, const float* b, float* out, int64_t rows,
+                 int64_t cols, int64_t ldb, int64_t ldo, b2g_stream_t stream);
+
+/* Read and clear the device-side error word of `device` (synchronises it). */
+B2G_API int b2g_read_device_error(int device, int32_t* code);
+
+/* Human-readable text for a b2g_status. */
+B2G_API const char* b2g_status_string(int status);
+
+/* Library version: major*10000 + minor*100 + patch. */
+B2G_API int b2g_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2G_GEMM_H */
