@@ -19,6 +19,8 @@ B2G_ERR_WORKSPACE = 3
 B2G_ERR_LAUNCH = 4
 B2G_ERR_DEVICE_TIMEOUT = 5
 B2G_ERR_NO_DEVICE = 6
+B2G_ERR_SCRATCH_LIMIT = 7
+NOALLOC_SCRATCH_BYTES = 16 << 20
 
 OP_GEMM, OP_TRI_UPPER, OP_TRI_LOWER = 0, 1, 2
 PREC_TF32, PREC_3XTF32 = 0, 1
@@ -60,6 +62,8 @@ def lib(path: Path | None = None) -> C.CDLL:
         h.b2g_gemm_workspace_bytes.restype = C.c_int64
         h.b2g_gemm.argtypes = [C.POINTER(GemmDesc), C.c_void_p]
         h.b2g_gemm.restype = C.c_int
+        h.b2g_gemm_noalloc.argtypes = [C.POINTER(GemmDesc), C.c_void_p]
+        h.b2g_gemm_noalloc.restype = C.c_int
         h.b2g_rowscale.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                    C.c_int64, C.c_int64, C.c_void_p]
         h.b2g_rowscale.restype = C.c_int
@@ -98,6 +102,11 @@ def plan(desc: GemmDesc, num_sms: int = 148) -> GemmPlan:
 
 def gemm(desc: GemmDesc, stream: int = 0) -> int:
     return lib().b2g_gemm(C.byref(desc), C.c_void_p(stream))
+
+
+def gemm_noalloc(desc: GemmDesc, stream: int = 0) -> int:
+    """b2g_gemm without any device allocation (fixed 16 MiB staging scratch)."""
+    return lib().b2g_gemm_noalloc(C.byref(desc), C.c_void_p(stream))
 
 
 def rowscale(d, b, out, rows, cols, ldb, ldo, stream: int = 0) -> int:

@@ -242,6 +242,8 @@ extern "C" const char* b2g_status_string(int s) {
     case B2G_ERR_LAUNCH: return "CUDA launch or API failure";
     case B2G_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
     case B2G_ERR_NO_DEVICE: return "no sm_100 device is current";
+    case B2G_ERR_SCRATCH_LIMIT:
+      return "operand staging needs more than the fixed no-allocation scratch (16 MiB)";
     default: return "unknown status";
   }
 }
@@ -299,25 +301,17 @@ extern "C" int64_t b2g_gemm_workspace_bytes(const b2g_gemm_desc* d) {
   return pl.workspace_bytes;
 }
 
-extern "C" int b2g_gemm(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {
-  if (!valid_desc(d)) return B2G_ERR_INVALID_ARG;
-  if (d->m == 0 || d->n == 0) return B2G_OK;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
-  DeviceState* ds = nullptr;
-  int rc = device_state(&ds);
-  if (rc != B2G_OK) return rc;
-  b2g_gemm_plan pl;
-  rc = b2g_gemm_plan_for(d, ds->num_sms, &pl);
-  if (rc != B2G_OK) return rc;
-  if (pl.workspace_bytes > 0 && (!d->workspace || d->workspace_bytes < pl.workspace_bytes))
-    return B2G_ERR_WORKSPACE;
-
+// Everything a GEMM call does once its plan is known and its workspace
+// checked: staged copies of unaligned operands, tensor maps, split-K clear
+// of C, and the engine launch.
+static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* workspace,
+                       int* err_word, cudaStream_t stream) {
   const float* a = d->a;
   const float* b = d->b;
   int64_t lda = d->lda, ldb = d->ldb, sa = d->stride_a, sb = d->stride_b;
   const int64_t a_batch = (d->stride_a == 0) ? 1 : d->batch;
   const int64_t b_batch = (d->stride_b == 0) ? 1 : d->batch;
-  char* ws = static_cast<char*>(d->workspace);
+  char* ws = static_cast<char*>(workspace);
   if (d->k > 0 && pl.stage_a) {
     Stage g = stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, a_batch);
     float* dst = reinterpret_cast<float*>(ws);
@@ -364,7 +358,7 @@ extern "C" int b2g_gemm(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {
   p.atomic_out = pl.splits > 1;
   p.vec_ok = (reinterpret_cast<uintptr_t>(d->c) % 16 == 0) && (d->ldc % 4 == 0) &&
              (d->batch == 1 || d->stride_c % 4 == 0);
-  p.err = ds->err_word;
+  p.err = err_word;
 
   if (p.atomic_out) {
     // Split-K accumulates into C: clear it first.
@@ -400,6 +394,21 @@ extern "C" int b2g_gemm(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {
   }
   if (tri) return launch_majors<128, 6, false, true>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
   return launch_majors<128, 6, false, false>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
+}
+
+extern "C" int b2g_gemm(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {
+  if (!valid_desc(d)) return B2G_ERR_INVALID_ARG;
+  if (d->m == 0 || d->n == 0) return B2G_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  DeviceState* ds = nullptr;
+  int rc = device_state(&ds);
+  if (rc != B2G_OK) return rc;
+  b2g_gemm_plan pl;
+  rc = b2g_gemm_plan_for(d, ds->num_sms, &pl);
+  if (rc != B2G_OK) return rc;
+  if (pl.workspace_bytes > 0 && (!d->workspace || d->workspace_bytes < pl.workspace_bytes))
+    return B2G_ERR_WORKSPACE;
+  return run_planned(d, pl, d->workspace, ds->err_word, stream);
 }
 
 extern "C" int b2g_rowscale(const float* d, const float* b, float* out, int64_t rows, int64_t cols,
@@ -449,4 +458,77 @@ extern "C" int b2g_read_device_error(int device, int32_t* code) {
   }
   cudaSetDevice(prev);
   return rc;
+}
+
+// ---------------------------------------------------------------- allocation-free entry point
+// b2g_gemm_noalloc serves callers that may not allocate device memory: a
+// plugin host that hands the library only its input and output buffers and
+// exposes no allocator (for instance a serving runtime whose memory pool
+// already owns the GPU's free memory, where a cudaMalloc would fail or
+// fragment that pool), or a latency-bound loop that cannot afford
+// cudaMalloc/cudaFree, which may synchronise the device.  Operands that need
+// a 16-byte-aligned staged copy are staged in this fixed file-scope array
+// instead of caller workspace.  Every GPU that loads this library holds the
+// array until the process exits.  All calls on a device share it and it
+// keeps the last call's contents; nothing in it has to start at zero (each
+// staged copy overwrites the bytes the engine reads), but calls whose work
+// overlaps on the GPU (different streams, no ordering between them) race on
+// it.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[B2G_NOALLOC_SCRATCH_BYTES];
+// Device error word of this path (bounded-wait timeouts); separate from the
+// word b2g_read_device_error reports, which b2g_gemm allocates on first use.
+static __device__ int g_noalloc_err;
+
+namespace {
+
+struct NoAllocDevice {
+  bool ready = false;
+  int num_sms = 0;
+  void* scratch = nullptr;      // device address of g_noalloc_scratch on this device
+  int* err = nullptr;           // device address of g_noalloc_err on this device
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc[kMaxDevices];
+
+// Once per device, with that device current: look up the device addresses
+// of the file-scope arrays.  The host-side names are only stand-ins; a
+// kernel must be given these addresses.  No allocation happens here.
+int noalloc_device(NoAllocDevice** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B2G_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  NoAllocDevice& st = g_noalloc[dev];
+  if (!st.ready) {
+    int major = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        major != 10)
+      return B2G_ERR_NO_DEVICE;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return B2G_ERR_NO_DEVICE;
+    void* scratch = nullptr;
+    void* err = nullptr;
+    if (cudaGetSymbolAddress(&scratch, g_noalloc_scratch) != cudaSuccess) return B2G_ERR_LAUNCH;
+    if (cudaGetSymbolAddress(&err, g_noalloc_err) != cudaSuccess) return B2G_ERR_LAUNCH;
+    st.num_sms = sms;
+    st.scratch = scratch;
+    st.err = static_cast<int*>(err);
+    st.ready = true;
+  }
+  *out = &st;
+  return B2G_OK;
+}
+
+}  // namespace
+
+extern "C" int b2g_gemm_noalloc(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {
+  if (!valid_desc(d)) return B2G_ERR_INVALID_ARG;
+  if (d->m == 0 || d->n == 0) return B2G_OK;
+  NoAllocDevice* st = nullptr;
+  int rc = noalloc_device(&st);
+  if (rc != B2G_OK) return rc;
+  b2g_gemm_plan pl;
+  rc = b2g_gemm_plan_for(d, st->num_sms, &pl);
+  if (rc != B2G_OK) return rc;
+  if (pl.workspace_bytes > B2G_NOALLOC_SCRATCH_BYTES) return B2G_ERR_SCRATCH_LIMIT;
+  return run_planned(d, pl, st->scratch, st->err, static_cast<cudaStream_t>(stream_handle));
 }

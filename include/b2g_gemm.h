@@ -60,7 +60,8 @@ typedef enum b2g_status {
   B2G_ERR_WORKSPACE = 3,        /* workspace missing or too small          */
   B2G_ERR_LAUNCH = 4,           /* CUDA launch / API call failed           */
   B2G_ERR_DEVICE_TIMEOUT = 5,   /* a bounded device-side wait gave up      */
-  B2G_ERR_NO_DEVICE = 6         /* no sm_100 device current                */
+  B2G_ERR_NO_DEVICE = 6,        /* no sm_100 device current                */
+  B2G_ERR_SCRATCH_LIMIT = 7     /* b2g_gemm_noalloc: staging exceeds its fixed scratch */
 } b2g_status;
 
 typedef enum b2g_op {
@@ -124,6 +125,35 @@ B2G_API int b2g_gemm(const b2g_gemm_desc* desc, b2g_stream_t stream);
  */
 B2G_API int b2g_rowscale(const float* d, const float* b, float* out, int64_t rows,
                  int64_t cols, int64_t ldb, int64_t ldo, b2g_stream_t stream);
+
+/*
+ * b2g_gemm_noalloc — b2g_gemm for callers that cannot allocate device memory.
+ * This entry point has no counterpart in the reference.
+ *
+ * Who needs it: a plugin host that gives the library only its input and
+ * output buffers and no allocator (e.g. a serving runtime whose memory pool
+ * already owns the GPU's free memory, so a cudaMalloc would fail or fragment
+ * it), or a latency-bound loop that cannot pay for cudaMalloc/cudaFree, which
+ * may synchronise the device.  It makes no cudaMalloc, cudaFree or other
+ * allocating call.
+ *
+ * Same descriptor and result as b2g_gemm; desc->workspace is ignored.
+ * Operands whose pitch needs a 16-byte-aligned staged copy are staged in a
+ * fixed file-scope device array of B2G_NOALLOC_SCRATCH_BYTES (16 MiB), which
+ * every GPU that loads the library holds until the process exits.  A
+ * descriptor needing more staging than that returns B2G_ERR_SCRATCH_LIMIT
+ * before any work is issued (b2g_gemm_workspace_bytes() tells how much it
+ * needs; aligned operands need none).
+ *
+ * The first call on a device, with that device current, looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture begins.  All calls on a device share the one array and
+ * it keeps the last call's contents: calls whose work may overlap on the GPU
+ * (unordered streams) race on it.  Bounded-wait timeouts in this path are
+ * recorded in a word of its own, which b2g_read_device_error does not read.
+ */
+#define B2G_NOALLOC_SCRATCH_BYTES (16ll << 20)
+B2G_API int b2g_gemm_noalloc(const b2g_gemm_desc* desc, b2g_stream_t stream);
 
 /* Read and clear the device-side error word of `device` (synchronises it). */
 B2G_API int b2g_read_device_error(int device, int32_t* code);
