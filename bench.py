@@ -313,6 +313,9 @@ def main():
     ap.add_argument("--no-shapes", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--shapes", default="", help="comma list restricting the per-shape table")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the per-GPU batch (profiling runs on a small case)")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -323,6 +326,12 @@ def main():
     peaks = load_peaks()
     W = _pkg("workloads").WORKLOADS
     w = W[HEADLINE]
+    if args.batch:
+        import dataclasses
+
+        shapes = dict(w.shapes, batch=args.batch)
+        flops, nbytes = _pkg("workloads").cost_for(HEADLINE, **shapes)
+        w = dataclasses.replace(w, shapes=shapes, flops=flops, min_bytes=nbytes)
     s = w.shapes
 
     if args.impl == "ours":
@@ -333,7 +342,7 @@ def main():
     else:
         op = None
 
-    A, B = device_inputs(w, seed_offset=rank)
+    A, B = device_inputs(w, seed_offset=rank, **s)
     if args.impl == "ours":
         fn = lambda: op(A, B)
         impl_note = None
@@ -367,6 +376,47 @@ def main():
     rl["peak_note"] = peaks["tf32_note"] if rl["bound"] == "tensor" else "MEASURED_PEAKS.json hbm_gbs"
 
     # ---- end to end through the public API, host buffers in the timed region
+    e2e = None if args.no_e2e else end_to_end(args, w, A, B, op, world)
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "tf32" if args.precision == "tf32" else "3xtf32 (fp32-grade)",
+        "data": "synthetic: N(0,1) fp32 from a per-rank seeded generator (no dataset)",
+        "config": {"workload": "batched (BASELINE configs[2]; reference PID 3)"
+                   + (f", batch overridden to {s['batch']}" if args.batch else ""),
+                   "batch_per_gpu": s["batch"], "m": s["m"], "k": s["k"], "n": s["n"],
+                   "global_batch": s["batch"] * world, "precision": args.precision,
+                   "parallelism": f"batch-sharded x{world}, no communication",
+                   "l2": f"inputs larger than L2 ({w.min_bytes / 1e9:.2f} GB touched per step)"},
+        "roofline": rl, "e2e": e2e, "clocks": clk,
+    }
+    if args.impl == "ours":
+        line["gpu_launches"] = launches_per_step * args.steps
+    else:
+        line["impl"] = "reference"
+        line["reference"] = ("kernels/3_Batched_matrix_multiplication_best_kernel.cu:113 "
+                             "batched_matmul_cuda, compiled unmodified for sm_100a")
+    if rank == 0 and world == 1 and args.impl == "ours" and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(w)
+    if rank == 0 and world == 1 and args.impl == "ours" and not args.no_shapes:
+        del A, B
+        torch.cuda.empty_cache()
+        only = set(x for x in args.shapes.split(",") if x)
+        line["shapes"] = shape_table(W, peaks, only, ops)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def end_to_end(args, w, A, B, op, world):
+    """The metric through the public API with pinned host inputs copied in and
+    the result copied out inside the timed region."""
+    s = w.shapes
     A_h = A.cpu().pin_memory()
     B_h = B.cpu().pin_memory()
     C_h = torch.empty(s["batch"], s["m"], s["n"], dtype=torch.float32).pin_memory()
@@ -390,40 +440,8 @@ def main():
            "ms_per_step": round(e2e_per, 3),
            "h2d_bytes_per_step": A.numel() * 4 + B.numel() * 4,
            "d2h_bytes_per_step": s["batch"] * s["m"] * s["n"] * 4}
-    del A_h, B_h, C_h, A_d, B_d
+    return e2e
 
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "tf32" if args.precision == "tf32" else "3xtf32 (fp32-grade)",
-        "data": "synthetic: N(0,1) fp32 from a per-rank seeded generator (no dataset)",
-        "config": {"workload": "batched (BASELINE configs[2]; reference PID 3)",
-                   "batch_per_gpu": s["batch"], "m": s["m"], "k": s["k"], "n": s["n"],
-                   "global_batch": s["batch"] * world, "precision": args.precision,
-                   "parallelism": f"batch-sharded x{world}, no communication",
-                   "l2": "inputs larger than L2 (1.88 GB touched per step)"},
-        "roofline": rl, "e2e": e2e, "clocks": clk,
-    }
-    if args.impl == "ours":
-        line["gpu_launches"] = launches_per_step * args.steps
-    else:
-        line["impl"] = "reference"
-        line["reference"] = ("kernels/3_Batched_matrix_multiplication_best_kernel.cu:113 "
-                             "batched_matmul_cuda, compiled unmodified for sm_100a")
-    if rank == 0 and world == 1 and args.impl == "ours" and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline(w)
-    if rank == 0 and world == 1 and args.impl == "ours" and not args.no_shapes:
-        del A, B
-        torch.cuda.empty_cache()
-        only = set(x for x in args.shapes.split(",") if x)
-        line["shapes"] = shape_table(W, peaks, only, ops)
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
 
 
 def shape_table(W, peaks, only, ops):

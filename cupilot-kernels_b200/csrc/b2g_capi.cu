@@ -154,11 +154,11 @@ __global__ void rowscale_scalar_kernel(const float* __restrict__ d, const float*
 }
 
 // ---------------------------------------------------------------- engine instantiations
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF>
-int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const EngineParams& p, int grid,
-                  cudaStream_t stream) {
-  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>;
-  auto kern = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, X3, XF>;
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR>
+int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                  const EngineParams& p, int grid, cudaStream_t stream) {
+  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR>;
+  auto kern = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, X3, XF, PAIR>;
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -168,17 +168,34 @@ int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const EnginePara
       return B2G_ERR_LAUNCH;
     configured_dev = dev;
   }
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (PAIR) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p) != cudaSuccess) return B2G_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
 }
 
-template <int BN, int STAGES, bool X3, bool XF>
+template <int BN, int STAGES, bool X3, bool XF, bool PAIR>
 int launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb,
-                  const EngineParams& p, int grid, cudaStream_t st) {
-  if (!a_mn && !b_mn) return launch_engine<BN, STAGES, false, false, X3, XF>(ma, mb, p, grid, st);
-  if (!a_mn && b_mn) return launch_engine<BN, STAGES, false, true, X3, XF>(ma, mb, p, grid, st);
-  if (a_mn && !b_mn) return launch_engine<BN, STAGES, true, false, X3, XF>(ma, mb, p, grid, st);
-  return launch_engine<BN, STAGES, true, true, X3, XF>(ma, mb, p, grid, st);
+                  const CUtensorMap& mc, const EngineParams& p, int grid, cudaStream_t st) {
+  if (!a_mn && !b_mn)
+    return launch_engine<BN, STAGES, false, false, X3, XF, PAIR>(ma, mb, mc, p, grid, st);
+  if (!a_mn && b_mn)
+    return launch_engine<BN, STAGES, false, true, X3, XF, PAIR>(ma, mb, mc, p, grid, st);
+  if (a_mn && !b_mn)
+    return launch_engine<BN, STAGES, true, false, X3, XF, PAIR>(ma, mb, mc, p, grid, st);
+  return launch_engine<BN, STAGES, true, true, X3, XF, PAIR>(ma, mb, mc, p, grid, st);
 }
 
 bool valid_desc(const b2g_gemm_desc* d) {
@@ -252,36 +269,62 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   if (!valid_desc(d) || !pl || num_sms <= 0) return B2G_ERR_INVALID_ARG;
   std::memset(pl, 0, sizeof(*pl));
   const bool x3 = d->precision == B2G_PREC_3XTF32;
-  const int64_t tiles_m = cdiv(d->m, kBlockM);
   const int64_t kb_total = cdiv(d->k, kBlockK);
   const int64_t batch = d->batch;
-  int bn;
+  int bn = 256, ctas = 1;
   if (x3) {
     bn = 128;
-  } else {
-    const int64_t t256 = tiles_m * cdiv(d->n, 256) * batch;
-    const int64_t t128 = tiles_m * cdiv(d->n, 128) * batch;
+  } else if (d->op != B2G_OP_GEMM) {
+    const int64_t tm = cdiv(d->m, kBlockM);
+    const int64_t t256 = tm * cdiv(d->n, 256) * batch;
+    const int64_t t128 = tm * cdiv(d->n, 128) * batch;
     bn = (t256 * 2 < num_sms && t128 > t256) ? 128 : 256;
+  } else {
+    // Cost model: waves of CTAs over the SMs times the per-SM tile work,
+    // divided by the per-SM efficiency of the tile shape (a CTA pair halves
+    // the B operand each SM streams through shared memory).
+    struct Cand { int ctas, bn; double eff; };
+    const Cand cands[] = {{2, 256, 1.0}, {2, 128, 0.95}, {1, 256, 0.8}, {1, 128, 0.7}};
+    double best = 0.0;
+    for (const Cand& c : cands) {
+      const int64_t units = cdiv(d->m, kBlockM * c.ctas) * cdiv(d->n, c.bn) * batch;
+      const double waves = static_cast<double>(cdiv(units * c.ctas, num_sms));
+      const double cost = waves * (kBlockM * c.bn) / c.eff;
+      if (best == 0.0 || cost < best * 0.999) {
+        best = cost;
+        bn = c.bn;
+        ctas = c.ctas;
+      }
+    }
   }
-  pl->block_m = kBlockM;
+  pl->block_m = kBlockM * ctas;
   pl->block_n = bn;
   pl->block_k = kBlockK;
-  pl->stages = x3 ? 3 : (bn == 256 ? 4 : 6);
-  pl->tiles_m = static_cast<int32_t>(tiles_m);
+  pl->cluster_ctas = ctas;
+  if (x3)
+    pl->stages = 3;
+  else if (ctas == 2)
+    pl->stages = bn == 256 ? 6 : 8;
+  else
+    pl->stages = bn == 256 ? 4 : 6;
+  pl->tiles_m = static_cast<int32_t>(cdiv(d->m, pl->block_m));
   pl->tiles_n = static_cast<int32_t>(cdiv(d->n, bn));
-  const int64_t tiles = tiles_m * pl->tiles_n * batch;
+  const int64_t tiles = static_cast<int64_t>(pl->tiles_m) * pl->tiles_n * batch;
+  const int64_t slots = tiles * ctas;
   int64_t splits = 1;
-  if (d->op == B2G_OP_GEMM && tiles > 0 && tiles * 4 < num_sms * 3 && kb_total >= 8) {
-    splits = std::max<int64_t>(1, std::min<int64_t>(num_sms / tiles, kb_total / 4));
+  if (d->op == B2G_OP_GEMM && slots > 0 && slots * 4 < num_sms * 3 && kb_total >= 8) {
+    splits = std::max<int64_t>(1, std::min<int64_t>(num_sms / slots, kb_total / 4));
   }
   int64_t kbps = std::max<int64_t>(1, cdiv(kb_total, splits));
   splits = std::max<int64_t>(1, cdiv(kb_total, kbps));
   pl->splits = static_cast<int32_t>(splits);
   pl->kb_per_split = static_cast<int32_t>(kbps);
   pl->work_units = tiles * splits;
-  pl->grid = static_cast<int32_t>(std::min<int64_t>(pl->work_units, num_sms));
+  pl->grid = static_cast<int32_t>(std::min<int64_t>(pl->work_units, num_sms / ctas) * ctas);
   pl->a_mn_major = d->trans_a ? 1 : 0;
   pl->b_mn_major = d->trans_b ? 0 : 1;
+  pl->tma_store = (reinterpret_cast<uintptr_t>(d->c) % 16 == 0) && (d->ldc % 4 == 0) &&
+                  (d->batch == 1 || d->stride_c % 4 == 0);
   const int64_t sa_batch = (d->stride_a == 0) ? 1 : batch;
   const int64_t sb_batch = (d->stride_b == 0) ? 1 : batch;
   pl->stage_a = tma_ok(d->a, d->lda, d->stride_a, sa_batch) ? 0 : 1;
@@ -341,6 +384,7 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.N = static_cast<int>(d->n);
   p.K = static_cast<int>(d->k);
   p.batch = static_cast<int>(d->batch);
+  p.block_m = pl.block_m;
   p.block_n = pl.block_n;
   p.tiles_m = pl.tiles_m;
   p.tiles_n = pl.tiles_n;
@@ -358,6 +402,7 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.atomic_out = pl.splits > 1;
   p.vec_ok = (reinterpret_cast<uintptr_t>(d->c) % 16 == 0) && (d->ldc % 4 == 0) &&
              (d->batch == 1 || d->stride_c % 4 == 0);
+  p.tma_store = pl.tma_store;
   p.err = err_word;
 
   if (p.atomic_out) {
@@ -369,8 +414,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     }
   }
 
-  CUtensorMap ma, mb;
-  const int bn = pl.block_n;
+  CUtensorMap ma, mb, mc;
+  const int bn_cta = pl.block_n / pl.cluster_ctas;
   const int64_t k_ext = std::max<int64_t>(d->k, 1);
   bool ok;
   if (!pl.a_mn_major)
@@ -379,21 +424,37 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     ok = make_map(&ma, a, d->m, k_ext, a_batch, lda, sa, 32, kBlockK, true);
   if (!ok) return B2G_ERR_UNSUPPORTED;
   if (!pl.b_mn_major)
-    ok = make_map(&mb, b, k_ext, d->n, b_batch, ldb, sb, kBlockK, bn, false);
+    ok = make_map(&mb, b, k_ext, d->n, b_batch, ldb, sb, kBlockK, bn_cta, false);
   else
     ok = make_map(&mb, b, d->n, k_ext, b_batch, ldb, sb, 32, kBlockK, true);
   if (!ok) return B2G_ERR_UNSUPPORTED;
+  if (pl.tma_store) {
+    // C boxes of 32 x 32 fp32, 128-byte swizzled like the epilogue's staging.
+    if (!make_map(&mc, d->c, d->n, d->m, d->batch, d->ldc, d->stride_c, 32, 32, false))
+      return B2G_ERR_UNSUPPORTED;
+  } else {
+    mc = ma;   // unused by the kernel
+  }
 
   const bool a_mn = pl.a_mn_major, b_mn = pl.b_mn_major;
   const bool x3 = d->precision == B2G_PREC_3XTF32;
   const bool tri = p.tri != kTriNone;
-  if (x3) return launch_majors<128, 3, true, true>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
-  if (bn == 256) {
-    if (tri) return launch_majors<256, 4, false, true>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
-    return launch_majors<256, 4, false, false>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
+  const int grid = pl.grid;
+  if (x3)
+    return launch_majors<128, 3, true, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+  if (pl.cluster_ctas == 2) {
+    if (pl.block_n == 256)
+      return launch_majors<256, 6, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+    return launch_majors<128, 8, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
   }
-  if (tri) return launch_majors<128, 6, false, true>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
-  return launch_majors<128, 6, false, false>(a_mn, b_mn, ma, mb, p, pl.grid, stream);
+  if (pl.block_n == 256) {
+    if (tri)
+      return launch_majors<256, 4, false, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+    return launch_majors<256, 4, false, false, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+  }
+  if (tri)
+    return launch_majors<128, 6, false, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+  return launch_majors<128, 6, false, false, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
 }
 
 extern "C" int b2g_gemm(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {

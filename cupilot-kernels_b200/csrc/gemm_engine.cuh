@@ -45,6 +45,7 @@ enum : int {
 
 struct EngineParams {
   int M, N, K, batch;
+  int block_m;                 // output rows per work unit (128, or 256 for a CTA pair)
   int block_n;
   int tiles_m, tiles_n;
   int splits, kb_total, kb_per_split;
@@ -54,8 +55,9 @@ struct EngineParams {
   long long work_units;
   float* C;
   long long ldc, stride_c;
-  int atomic_out;
-  int vec_ok;
+  int atomic_out;              // split-K: accumulate into a cleared C
+  int vec_ok;                  // C rows 16-byte aligned (direct-store path)
+  int tma_store;               // write C with TMA tensor stores (reduce-add for split-K)
   int* err;
 };
 
@@ -87,7 +89,7 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
   int hi = lo + p.kb_per_split;
   if (hi > p.kb_total) hi = p.kb_total;
   if (p.tri != kTriNone) {
-    const long long m0 = static_cast<long long>(u.tm) * kBlockM;
+    const long long m0 = static_cast<long long>(u.tm) * p.block_m;
     const long long n0 = static_cast<long long>(u.tn) * p.block_n;
     long long klo, khi;
     if (p.tri == kTriUpper) {  // k in [i, j]
@@ -96,8 +98,8 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
       if (n0 + p.block_n - 1 < m0) khi = klo;       // tile wholly below the diagonal
     } else {                   // k in [j, i]
       klo = n0;
-      khi = m0 + kBlockM;
-      if (n0 > m0 + kBlockM - 1) khi = klo;          // tile wholly above the diagonal
+      khi = m0 + p.block_m;
+      if (n0 > m0 + p.block_m - 1) khi = klo;        // tile wholly above the diagonal
     }
     if (khi > p.K) khi = p.K;
     int tlo = static_cast<int>(klo / kBlockK);
@@ -111,29 +113,38 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
   return u;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF>
+// PAIR: a cluster of two CTAs computes one 256 x BN unit with
+// tcgen05.mma.cta_group::2; each CTA holds 128 rows of A, BN/2 columns of B
+// and its 128 x BN half of the accumulator.
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR>
 struct EngineCfg {
+  static constexpr int kCtas = PAIR ? 2 : 1;
+  static constexpr int kUnitM = kBlockM * kCtas;
+  static constexpr int kBnCta = BN / kCtas;                 // B columns loaded per CTA
   static constexpr int kABytes = kBlockM * kBlockK * 4;
-  static constexpr int kBBytes = BN * kBlockK * 4;
-  static constexpr int kStageTx = kABytes + kBBytes;
+  static constexpr int kBBytes = kBnCta * kBlockK * 4;
+  static constexpr int kStageTx = kABytes + kBBytes;        // bytes per CTA per stage
   static constexpr int kOperandBufs = X3 ? 2 : 1;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = STAGES * kABytes;
   static constexpr int kOffALo = STAGES * (kABytes + kBBytes);
   static constexpr int kOffBLo = kOffALo + STAGES * kABytes;
   static constexpr int kOffEpi = STAGES * (kABytes + kBBytes) * kOperandBufs;
-  static constexpr int kEpiWarps = 4;
-  static constexpr int kEpiBytes = kEpiWarps * 32 * 32 * 4;
+  static constexpr int kEpiWarps = 8;                        // two per TMEM lane quadrant
+  static constexpr int kEpiBufBytes = 32 * 32 * 4;           // one 32 x 32 fp32 box
+  static constexpr int kEpiBytes = kEpiWarps * kEpiBufBytes;
   static constexpr int kOffBar = kOffEpi + kEpiBytes;
   static constexpr int kNumBars = 3 * STAGES + 4;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kThreads = XF ? 320 : 192;
+  static constexpr int kXformWarps = XF ? 4 : 0;
+  static constexpr int kThreads = (2 + kEpiWarps + kXformWarps) * 32;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
-  static_assert(BN % 32 == 0 && BN <= 256, "BN");
+  static_assert(BN % 64 == 0 && BN <= 256, "BN");
   static_assert(!X3 || XF, "the 3xTF32 split runs in the transform warps");
+  static_assert(!(PAIR && XF), "transform warps run in single-CTA units only");
 };
 
 __device__ __forceinline__ void record_error(int* err, volatile int* abort, int code) {
@@ -238,11 +249,78 @@ __device__ __forceinline__ void store4(const EngineParams& p, float* crow, int g
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF>
-__global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kThreads, 1)
+// Wait for the asynchronous tcgen05.ld results, and pin every register of
+// `r` behind that wait so the compiler cannot read them earlier.
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
+  ptx::tmem_ld_wait();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+// One 32-row x 32-column accumulator chunk held by a warp (row = lane) to
+// global memory.  TMA path: swizzled 4 KB staging box -> tensor store (or
+// fp32 add-reduction for split-K); otherwise a swizzled transpose and
+// coalesced (or scalar, or atomic) stores.
+__device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtensorMap* map_c,
+                                            float* stg, uint32_t (&r)[32], int b, int row0,
+                                            int col0, int lane) {
+  const int row = row0 + lane;
+  if (p.tri == kTriUpper) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < row) r[j] = 0u;
+  } else if (p.tri == kTriLower) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j > row) r[j] = 0u;
+  }
+  if (p.tma_store) {
+    float* buf = stg;
+    if (lane == 0) ptx::bulk_wait_read<0>();   // the previous store has read the buffer
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(buf + lane * 32 + ((j ^ (lane & 7)) * 4)) =
+          make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                      __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (p.atomic_out)
+        ptx::tma_reduce_add_3d(map_c, buf, col0, row0, b);
+      else
+        ptx::tma_store_3d(map_c, buf, col0, row0, b);
+      ptx::bulk_commit();
+    }
+    return;
+  }
+  float* cb = p.C + static_cast<long long>(b) * p.stride_c;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<float4*>(stg + lane * 32 + ((j ^ (lane & 7)) * 4)) =
+        make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                    __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r_local = it * 4 + (lane >> 3);
+    const int jj = lane & 7;
+    const float4 v =
+        *reinterpret_cast<const float4*>(stg + r_local * 32 + ((jj ^ (r_local & 7)) * 4));
+    const int grow = row0 + r_local;
+    const int gcol = col0 + jj * 4;
+    if (grow < p.M && gcol < p.N)
+      store4(p, cb + static_cast<long long>(grow) * p.ldc, grow, gcol, v.x, v.y, v.z, v.w);
+  }
+  __syncwarp();
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR>
+__global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR>::kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a,
-                     const __grid_constant__ CUtensorMap map_b, const EngineParams p) {
-  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>;
+                     const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ CUtensorMap map_c, const EngineParams p) {
+  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -258,16 +336,20 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kTh
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? ptx::cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const long long unit0 = PAIR ? (blockIdx.x >> 1) : blockIdx.x;
+  const long long unit_step = PAIR ? (gridDim.x >> 1) : gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
-      ptx::mbar_init(&ready[s], 4);
+      ptx::mbar_init(&ready[s], Cfg::kXformWarps > 0 ? Cfg::kXformWarps : 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&tmem_full[b], 1);
-      ptx::mbar_init(&tmem_empty[b], Cfg::kEpiWarps);
+      ptx::mbar_init(&tmem_empty[b], Cfg::kEpiWarps * Cfg::kCtas);
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -275,25 +357,33 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kTh
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&map_a);
     ptx::prefetch_tmap(&map_b);
+    if (p.tma_store) ptx::prefetch_tmap(&map_c);
   }
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
-    ptx::tmem_relinquish();
+    if (PAIR) {
+      ptx::tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+      ptx::tmem_relinquish();
+    }
   }
   ptx::tc_fence_before();
   __syncthreads();
+  if (PAIR) ptx::cluster_sync();   // peer barriers initialised before any remote arrive
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      const uint32_t full_leader = PAIR ? ptx::mapa_shared(ptx::smem_addr(full), 0) : 0u;
       uint32_t it = 0;
       bool ok = true;
-      for (long long w = blockIdx.x; w < p.work_units && ok; w += gridDim.x) {
+      for (long long w = unit0; w < p.work_units && ok; w += unit_step) {
         const WorkUnit u = decode_unit(p, w);
-        const int m0 = u.tm * kBlockM;
-        const int n0 = u.tn * BN;
+        const int m_cta = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM;
+        const int n_cta = u.tn * BN + static_cast<int>(rank) * Cfg::kBnCta;
         const int ab = p.a_batched ? u.b : 0;
         const int bb = p.b_batched ? u.b : 0;
         for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
@@ -304,33 +394,40 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kTh
             ok = false;
             break;
           }
-          ptx::mbar_arrive_expect_tx(&full[s], Cfg::kStageTx);
+          if (!PAIR)
+            ptx::mbar_arrive_expect_tx(&full[s], Cfg::kStageTx);
+          else if (leader)
+            ptx::mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageTx);
           uint8_t* sa = smem + Cfg::kOffA + s * Cfg::kABytes;
           uint8_t* sb = smem + Cfg::kOffB + s * Cfg::kBBytes;
           const int k0 = kb * kBlockK;
+          auto load = [&](void* dst, const CUtensorMap* map, int c0, int c1, int c2) {
+            if (PAIR)
+              ptx::tma_load_3d_pair(dst, map, full_leader + s * 8, c0, c1, c2);
+            else
+              ptx::tma_load_3d(dst, map, &full[s], c0, c1, c2);
+          };
           if (!A_MN) {
-            ptx::tma_load_3d(sa, &map_a, &full[s], k0, m0, ab);
+            load(sa, &map_a, k0, m_cta, ab);
           } else {
 #pragma unroll
             for (int j = 0; j < kBlockM / 32; ++j)
-              ptx::tma_load_3d(sa + j * kBlockK * kSwRowBytes, &map_a, &full[s], m0 + 32 * j, k0,
-                               ab);
+              load(sa + j * kBlockK * kSwRowBytes, &map_a, m_cta + 32 * j, k0, ab);
           }
           if (!B_MN) {
-            ptx::tma_load_3d(sb, &map_b, &full[s], k0, n0, bb);
+            load(sb, &map_b, k0, n_cta, bb);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 32; ++j)
-              ptx::tma_load_3d(sb + j * kBlockK * kSwRowBytes, &map_b, &full[s], n0 + 32 * j, k0,
-                               bb);
+            for (int j = 0; j < Cfg::kBnCta / 32; ++j)
+              load(sb + j * kBlockK * kSwRowBytes, &map_b, n_cta + 32 * j, k0, bb);
           }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = ptx::idesc_tf32(kBlockM, BN, A_MN, B_MN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = ptx::idesc_tf32(Cfg::kUnitM, BN, A_MN, B_MN);
       // Canonical layouts (byte offsets).  K-major (128-byte swizzle): rows
       // 128 B apart, 8-row atoms 1024 B apart (SBO), LBO unused; a K=8 step
       // advances 32 B inside the row.  MN-major (32-byte-atom swizzle):
@@ -346,7 +443,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kTh
       constexpr uint32_t b_kstep = B_MN ? 8 * kSwRowBytes : 8 * 4;
       uint32_t it = 0, tl = 0;
       bool ok = true;
-      for (long long w = blockIdx.x; w < p.work_units && ok; w += gridDim.x) {
+      for (long long w = unit0; w < p.work_units && ok; w += unit_step) {
         const WorkUnit u = decode_unit(p, w);
         if (u.kb_lo >= u.kb_hi) continue;
         const int buf = tl & 1;
@@ -376,7 +473,10 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kTh
           for (int k8 = 0; k8 < kBlockK / 8; ++k8) {
             const uint64_t da = ptx::smem_desc(sa + k8 * a_kstep, a_lbo, a_sbo, a_lay);
             const uint64_t db = ptx::smem_desc(sb + k8 * b_kstep, b_lbo, b_sbo, b_lay);
-            ptx::mma_tf32(d_tmem, da, db, idesc, acc);
+            if (PAIR)
+              ptx::mma_tf32_pair(d_tmem, da, db, idesc, acc);
+            else
+              ptx::mma_tf32(d_tmem, da, db, idesc, acc);
             acc = 1;
             if (X3) {
               const uint64_t dal = ptx::smem_desc(sal + k8 * a_kstep, a_lbo, a_sbo, a_lay);
@@ -385,31 +485,42 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kTh
               ptx::mma_tf32(d_tmem, dal, db, idesc, 1);
             }
           }
-          ptx::mma_commit(&empty[s]);
+          if (PAIR)
+            ptx::mma_commit_pair(&empty[s], 0x3);
+          else
+            ptx::mma_commit(&empty[s]);
         }
         if (!ok) break;
-        ptx::mma_commit(&tmem_full[buf]);
+        if (PAIR)
+          ptx::mma_commit_pair(&tmem_full[buf], 0x3);
+        else
+          ptx::mma_commit(&tmem_full[buf]);
         ++tl;
       }
     }
   } else if (warp < 2 + Cfg::kEpiWarps) {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;                  // TMEM lane quadrant this warp may read
-    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffEpi) + (warp - 2) * 32 * 32;
+    // Warp e (0..7) reads TMEM lane quadrant warp % 4 (the hardware rule)
+    // and every other 32-column chunk starting at e / 4.
+    const int quad = warp & 3;
+    const int ew = warp - 2;
+    const int half = ew >> 2;
+    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffEpi) + ew * 32 * 32;
+    const uint32_t tmem_empty_leader =
+        PAIR ? ptx::mapa_shared(ptx::smem_addr(tmem_empty), 0) : 0u;
     uint32_t tl = 0;
-    for (long long w = blockIdx.x; w < p.work_units; w += gridDim.x) {
+    for (long long w = unit0; w < p.work_units; w += unit_step) {
       const WorkUnit u = decode_unit(p, w);
-      const int m0 = u.tm * kBlockM;
+      const int row0 = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM + quad * 32;
       const int n0 = u.tn * BN;
-      const int row_base = m0 + quad * 32;
-      float* cb = p.C + static_cast<long long>(u.b) * p.stride_c;
       if (u.kb_lo >= u.kb_hi) {
         // Structurally zero tile (or K == 0): write zeros unless accumulating.
-        if (!p.atomic_out && row_base < p.M) {
-          for (int it = 0; it < 8 * (BN / 32); ++it) {
+        if (!p.atomic_out && row0 < p.M) {
+          float* cb = p.C + static_cast<long long>(u.b) * p.stride_c;
+          for (int it = 0; it < 8 * (BN / 64); ++it) {
             const int r_local = (it & 7) * 4 + (lane >> 3);
-            const int gcol = n0 + (it >> 3) * 32 + (lane & 7) * 4;
-            const int grow = row_base + r_local;
+            const int gcol = n0 + ((it >> 3) * 2 + half) * 32 + (lane & 7) * 4;
+            const int grow = row0 + r_local;
             if (grow < p.M && gcol < p.N)
               store4(p, cb + static_cast<long long>(grow) * p.ldc, grow, gcol, 0.f, 0.f, 0.f, 0.f);
           }
@@ -423,52 +534,51 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kTh
         break;
       }
       ptx::tc_fence_after();
-      if (row_base < p.M) {
-#pragma unroll 1
-        for (int ch = 0; ch < BN / 32; ++ch) {
-          const int col0 = n0 + ch * 32;
-          if (col0 >= p.N) break;
-          uint32_t r[32];
-          ptx::tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                      buf * BN + ch * 32,
-                                  r);
-          ptx::tmem_ld_wait();
-          // Row `lane` of this warp's 32x32 block -> swizzled staging row.
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4* dst = reinterpret_cast<float4*>(stg + lane * 32 + ((j ^ (lane & 7)) * 4));
-            *dst = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-          }
-          __syncwarp();
-          // 8 lanes cover one 128-byte row segment: coalesced stores.
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int r_local = it * 4 + (lane >> 3);
-            const int jj = lane & 7;
-            const float4 v =
-                *reinterpret_cast<const float4*>(stg + r_local * 32 + ((jj ^ (r_local & 7)) * 4));
-            const int grow = row_base + r_local;
-            const int gcol = col0 + jj * 4;
-            if (grow < p.M && gcol < p.N)
-              store4(p, cb + static_cast<long long>(grow) * p.ldc, grow, gcol, v.x, v.y, v.z, v.w);
-          }
-          __syncwarp();
+      auto release = [&]() {
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (PAIR)
+            ptx::mbar_arrive_cluster(tmem_empty_leader + buf * 8);
+          else
+            ptx::mbar_arrive(&tmem_empty[buf]);
         }
+      };
+      int nch = (p.N - n0 + 31) / 32;
+      if (nch > BN / 32) nch = BN / 32;
+      if (row0 < p.M && half < nch) {
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
+        uint32_t ra[32], rb[32];
+        ptx::tmem_ld_32x32b_x32(taddr + half * 32, ra);
+        tmem_ld_wait_regs(ra);
+#pragma unroll 1
+        for (int ch = half; ch < nch; ch += 2) {
+          const bool more = ch + 2 < nch;
+          if (more)
+            ptx::tmem_ld_32x32b_x32(taddr + (ch + 2) * 32, rb);   // in flight while ra drains
+          else
+            release();                                            // every TMEM read is done
+          store_chunk(p, &map_c, stg, ra, u.b, row0, n0 + ch * 32, lane);
+          if (more) {
+            tmem_ld_wait_regs(rb);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ra[i] = rb[i];
+          }
+        }
+      } else {
+        release();
       }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&tmem_empty[buf]);
       ++tl;
     }
+    if (lane == 0) ptx::bulk_wait_all();
   } else if (XF) {
     // ------------------------------------------------------------ transform
     const int xt = threadIdx.x - (2 + Cfg::kEpiWarps) * 32;
     uint32_t it = 0;
     bool ok = true;
-    for (long long w = blockIdx.x; w < p.work_units && ok; w += gridDim.x) {
+    for (long long w = unit0; w < p.work_units && ok; w += unit_step) {
       const WorkUnit u = decode_unit(p, w);
-      const int m0 = u.tm * kBlockM;
+      const int m0 = u.tm * Cfg::kUnitM;
       const int n0 = u.tn * BN;
       for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
         const int s = it % STAGES;
@@ -502,9 +612,13 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF>::kTh
 
   ptx::tc_fence_before();
   __syncthreads();
+  if (PAIR) ptx::cluster_sync();   // no CTA leaves while its peer may still signal it
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    if (PAIR)
+      ptx::tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    else
+      ptx::tmem_dealloc(tmem_base, Cfg::kTmemCols);
   }
 }
 

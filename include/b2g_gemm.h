@@ -98,7 +98,7 @@ typedef struct b2g_gemm_desc {
 
 /* What the host dispatcher chose for a descriptor (pure host computation). */
 typedef struct b2g_gemm_plan {
-  int32_t block_m, block_n, block_k;
+  int32_t block_m, block_n, block_k;   /* block_m: output rows per work unit */
   int32_t stages;
   int32_t tiles_m, tiles_n;
   int32_t splits;               /* split-K factor; >1 accumulates into a zeroed C */
@@ -106,6 +106,8 @@ typedef struct b2g_gemm_plan {
   int32_t grid;                 /* persistent CTAs launched                */
   int32_t stage_a, stage_b;     /* 1: operand copied to a 16-byte-aligned pitch in workspace */
   int32_t a_mn_major, b_mn_major;
+  int32_t cluster_ctas;         /* 2: a CTA pair computes each 256-row unit (tcgen05 cta_group::2) */
+  int32_t tma_store;            /* 1: C written by TMA tensor stores (C rows 16-byte aligned) */
   int64_t work_units;
   int64_t workspace_bytes;
 } b2g_gemm_plan;

@@ -40,7 +40,7 @@ def test_version_and_status_strings(capi):
 def test_struct_layout_matches_header(capi):
     # 2 x int32 + 4 x int64 + 3 x (ptr, int64, int64, int32->padded) ... checked by size.
     assert ctypes.sizeof(capi.GemmDesc) == 8 + 32 + 3 * 32 - 8 + 16
-    assert ctypes.sizeof(capi.GemmPlan) == 13 * 4 + 4 + 16
+    assert ctypes.sizeof(capi.GemmPlan) == 15 * 4 + 4 + 16
 
 
 ALIGNED = 1 << 20   # a fake 16-byte-aligned device address: planning never dereferences
@@ -55,29 +55,46 @@ def _plan(capi, m, n, k, **kw):
 
 def test_plan_square_2048(capi):
     p = _plan(capi, 2048, 2048, 2048)
-    assert (p.block_m, p.block_n, p.block_k) == (128, 256, 32)
-    assert p.splits == 1 and p.tiles_m == 16 and p.tiles_n == 8
-    assert p.grid == 128 and p.work_units == 128
+    # CTA pairs on 256 x 256 units: 64 units on 128 SMs, one wave.
+    assert (p.block_m, p.block_n, p.block_k) == (256, 256, 32)
+    assert p.cluster_ctas == 2 and p.stages == 6
+    assert p.splits == 1 and p.tiles_m == 8 and p.tiles_n == 8
+    assert p.grid == 128 and p.work_units == 64
     assert p.a_mn_major == 0 and p.b_mn_major == 1
     assert p.stage_a == 0 and p.stage_b == 0 and p.workspace_bytes == 0
+    assert p.tma_store == 1
 
 
 def test_plan_transposes_set_majorness(capi):
     p = _plan(capi, 1024, 2048, 4096, trans_a=1, trans_b=1)
     assert p.a_mn_major == 1 and p.b_mn_major == 0
-    assert p.block_n == 128            # 64 tiles of 256 would leave half the SMs idle
+    # 256 x 256 units would fill 64 SMs; 256 x 128 units fill 128.
+    assert p.cluster_ctas == 2 and p.block_n == 128 and p.grid == 128
+
+
+def test_plan_grid_is_even_for_pairs(capi):
+    for m, n, k in [(256, 256, 256), (4096, 4096, 64), (300, 5000, 100), (8205, 5921, 2949)]:
+        p = _plan(capi, m, n, k, a=ALIGNED, b=ALIGNED)
+        if p.cluster_ctas == 2:
+            assert p.grid % 2 == 0 and p.grid <= 148
+
+
+def test_plan_unaligned_output_disables_tma_store(capi):
+    p = _plan(capi, 100, 101, 64, ldc=101)
+    assert p.tma_store == 0
 
 
 def test_plan_large_k_splits(capi):
     p = _plan(capi, 256, 256, 262144)
     assert p.splits > 1
-    assert p.work_units <= 148 and p.work_units >= 100
+    slots = p.work_units * p.cluster_ctas
+    assert 100 <= slots <= 148
     assert p.kb_per_split * p.splits >= 262144 // 32
 
 
 def test_plan_triangular_never_splits(capi):
     p = _plan(capi, 256, 256, 256, op=capi.OP_TRI_UPPER)
-    assert p.splits == 1
+    assert p.splits == 1 and p.cluster_ctas == 1
 
 
 def test_plan_irregular_stages_unaligned_operands(capi):
@@ -98,13 +115,14 @@ def test_plan_misaligned_base_pointer_is_staged(capi):
 
 def test_plan_3xtf32_uses_narrow_tiles(capi):
     p = _plan(capi, 2048, 2048, 2048, precision=capi.PREC_3XTF32)
-    assert p.block_n == 128 and p.stages == 3
+    assert p.block_n == 128 and p.stages == 3 and p.cluster_ctas == 1
 
 
 def test_plan_batched(capi):
     p = _plan(capi, 512, 2048, 1024, batch=128, stride_a=512 * 1024, stride_b=1024 * 2048,
               stride_c=512 * 2048)
-    assert p.work_units == 4 * 8 * 128 and p.grid == 148 and p.splits == 1
+    assert p.cluster_ctas == 2 and p.block_m == 256
+    assert p.work_units == 2 * 8 * 128 and p.grid == 148 and p.splits == 1
 
 
 @pytest.mark.parametrize("bad", [
