@@ -375,6 +375,13 @@ def main():
     rl["peak_source"] = peaks["source"]
     rl["peak_note"] = peaks["tf32_note"] if rl["bound"] == "tensor" else "MEASURED_PEAKS.json hbm_gbs"
 
+    cublas = None
+    if args.impl == "ours" and world == 1:
+        cb = cublas_fn(HEADLINE, A, B)
+        _, cb_ms = time_loop(cb, min(args.steps, 100), args.warmup)
+        cublas = {"ms": round(cb_ms, 4), "tflops": round(w.flops / (cb_ms / 1e3) / 1e12, 2),
+                  "what": "torch.matmul (cuBLAS) with TF32 allowed, same inputs, same GPU"}
+
     # ---- end to end through the public API, host buffers in the timed region
     e2e = None if args.no_e2e else end_to_end(args, w, A, B, op, world)
 
@@ -392,6 +399,8 @@ def main():
                    "l2": f"inputs larger than L2 ({w.min_bytes / 1e9:.2f} GB touched per step)"},
         "roofline": rl, "e2e": e2e, "clocks": clk,
     }
+    if cublas:
+        line["cublas_tf32"] = cublas
     if args.impl == "ours":
         line["gpu_launches"] = launches_per_step * args.steps
     else:

@@ -11,6 +11,8 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -265,6 +267,22 @@ extern "C" const char* b2g_status_string(int s) {
   }
 }
 
+namespace {
+
+// Split-K for a tile grid: split when the tiles alone leave more than a
+// quarter of the SMs idle, keeping at least 8 K blocks per split (partial
+// sums add into a cleared C).  Triangular ops never split.
+void choose_splits(const b2g_gemm_desc* d, int64_t slots, int64_t kb_total, int num_sms,
+                   int64_t* splits, int64_t* kbps) {
+  int64_t s = 1;
+  if (d->op == B2G_OP_GEMM && slots > 0 && slots * 4 < num_sms * 3 && kb_total >= 16)
+    s = std::max<int64_t>(1, std::min<int64_t>(num_sms / slots, kb_total / 8));
+  *kbps = std::max<int64_t>(1, cdiv(kb_total, s));
+  *splits = std::max<int64_t>(1, cdiv(kb_total, *kbps));
+}
+
+}  // namespace
+
 extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_plan* pl) {
   if (!valid_desc(d) || !pl || num_sms <= 0) return B2G_ERR_INVALID_ARG;
   std::memset(pl, 0, sizeof(*pl));
@@ -280,16 +298,29 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
     const int64_t t128 = tm * cdiv(d->n, 128) * batch;
     bn = (t256 * 2 < num_sms && t128 > t256) ? 128 : 256;
   } else {
-    // Cost model: waves of CTAs over the SMs times the per-SM tile work,
-    // divided by the per-SM efficiency of the tile shape (a CTA pair halves
-    // the B operand each SM streams through shared memory).
+    // Cost model: waves of CTAs over the SMs times the per-SM work of one
+    // unit (tile width x K blocks of its split), divided by the per-SM
+    // efficiency of the tile shape.  Efficiencies are measured throughputs
+    // on B200 relative to the CTA-pair 256 x 256 unit (8192 x 8192 x 4096:
+    // 712 / 590 / 474 / 452 TFLOP/s): wider units stream fewer operand
+    // bytes from L2 per flop, which is what bounds these kernels, so narrow
+    // tiles rarely pay even when they fill more SMs.
     struct Cand { int ctas, bn; double eff; };
-    const Cand cands[] = {{2, 256, 1.0}, {2, 128, 0.95}, {1, 256, 0.8}, {1, 128, 0.7}};
+    const Cand cands[] = {{2, 256, 1.0}, {1, 256, 0.83}, {2, 128, 0.66}, {1, 128, 0.63}};
+    // B2G_TILE=pair256|pair128|single256|single128 pins the choice (tuning aid).
+    static const char* forced = std::getenv("B2G_TILE");
     double best = 0.0;
     for (const Cand& c : cands) {
+      if (forced && *forced) {
+        char name[16];
+        std::snprintf(name, sizeof(name), "%s%d", c.ctas == 2 ? "pair" : "single", c.bn);
+        if (std::strcmp(name, forced) != 0) continue;
+      }
       const int64_t units = cdiv(d->m, kBlockM * c.ctas) * cdiv(d->n, c.bn) * batch;
-      const double waves = static_cast<double>(cdiv(units * c.ctas, num_sms));
-      const double cost = waves * (kBlockM * c.bn) / c.eff;
+      int64_t splits, kbps;
+      choose_splits(d, units * c.ctas, kb_total, num_sms, &splits, &kbps);
+      const double waves = static_cast<double>(cdiv(units * splits * c.ctas, num_sms));
+      const double cost = waves * c.bn * static_cast<double>(std::max<int64_t>(kbps, 1)) / c.eff;
       if (best == 0.0 || cost < best * 0.999) {
         best = cost;
         bn = c.bn;
@@ -310,13 +341,8 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   pl->tiles_m = static_cast<int32_t>(cdiv(d->m, pl->block_m));
   pl->tiles_n = static_cast<int32_t>(cdiv(d->n, bn));
   const int64_t tiles = static_cast<int64_t>(pl->tiles_m) * pl->tiles_n * batch;
-  const int64_t slots = tiles * ctas;
-  int64_t splits = 1;
-  if (d->op == B2G_OP_GEMM && slots > 0 && slots * 4 < num_sms * 3 && kb_total >= 8) {
-    splits = std::max<int64_t>(1, std::min<int64_t>(num_sms / slots, kb_total / 4));
-  }
-  int64_t kbps = std::max<int64_t>(1, cdiv(kb_total, splits));
-  splits = std::max<int64_t>(1, cdiv(kb_total, kbps));
+  int64_t splits, kbps;
+  choose_splits(d, tiles * ctas, kb_total, num_sms, &splits, &kbps);
   pl->splits = static_cast<int32_t>(splits);
   pl->kb_per_split = static_cast<int32_t>(kbps);
   pl->work_units = tiles * splits;

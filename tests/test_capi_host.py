@@ -68,8 +68,8 @@ def test_plan_square_2048(capi):
 def test_plan_transposes_set_majorness(capi):
     p = _plan(capi, 1024, 2048, 4096, trans_a=1, trans_b=1)
     assert p.a_mn_major == 1 and p.b_mn_major == 0
-    # 256 x 256 units would fill 64 SMs; 256 x 128 units fill 128.
-    assert p.cluster_ctas == 2 and p.block_n == 128 and p.grid == 128
+    # 32 units of 256 x 256 fill 64 SMs: K is split in two to fill 128.
+    assert p.cluster_ctas == 2 and p.block_n == 256 and p.splits == 2 and p.grid == 128
 
 
 def test_plan_grid_is_even_for_pairs(capi):
