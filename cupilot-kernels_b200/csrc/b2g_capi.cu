@@ -19,6 +19,10 @@
 #include "../../include/b2g_gemm.h"
 #include "gemm_engine.cuh"
 
+#ifndef B2G_PAIR256_STAGES
+#define B2G_PAIR256_STAGES 6   // pipeline depth of the CTA-pair 256-wide engine
+#endif
+
 namespace b2g {
 namespace {
 
@@ -93,6 +97,31 @@ bool make_map(CUtensorMap* map, const float* base, int64_t inner, int64_t outer,
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// MN-major operand (element (k, mn) at base + k*ld + mn) as a rank-4 map
+// {32, K, MN/32, batch}: one box {32, 32, groups, 1} lands all of a stage's
+// 32-wide groups in the layout the MMA reads (groups kBlockK*128 B apart).
+// Only for MN a multiple of 32, so the grouped view never reaches past the
+// operand's last row.  Returns false if the driver rejects the layout.
+bool make_map_grouped(CUtensorMap* map, const float* base, int64_t mn, int64_t k, int64_t batch,
+                      int64_t ld, int64_t bstride, uint32_t groups) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || mn % 32 != 0) return false;
+  if (batch <= 1) {
+    batch = 1;
+    bstride = round_up(ld * k, 4);
+  }
+  cuuint64_t dims[4] = {32, static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(mn / 32),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(ld) * 4, 128,
+                           static_cast<cuuint64_t>(bstride) * 4};
+  cuuint32_t box[4] = {32, static_cast<cuuint32_t>(kBlockK), groups, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -444,15 +473,19 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   const int bn_cta = pl.block_n / pl.cluster_ctas;
   const int64_t k_ext = std::max<int64_t>(d->k, 1);
   bool ok;
-  if (!pl.a_mn_major)
+  if (!pl.a_mn_major) {
     ok = make_map(&ma, a, k_ext, d->m, a_batch, lda, sa, kBlockK, kBlockM, false);
-  else
-    ok = make_map(&ma, a, d->m, k_ext, a_batch, lda, sa, 32, kBlockK, true);
+  } else {
+    p.a_grouped = make_map_grouped(&ma, a, d->m, k_ext, a_batch, lda, sa, kBlockM / 32);
+    ok = p.a_grouped || make_map(&ma, a, d->m, k_ext, a_batch, lda, sa, 32, kBlockK, true);
+  }
   if (!ok) return B2G_ERR_UNSUPPORTED;
-  if (!pl.b_mn_major)
+  if (!pl.b_mn_major) {
     ok = make_map(&mb, b, k_ext, d->n, b_batch, ldb, sb, kBlockK, bn_cta, false);
-  else
-    ok = make_map(&mb, b, d->n, k_ext, b_batch, ldb, sb, 32, kBlockK, true);
+  } else {
+    p.b_grouped = make_map_grouped(&mb, b, d->n, k_ext, b_batch, ldb, sb, bn_cta / 32);
+    ok = p.b_grouped || make_map(&mb, b, d->n, k_ext, b_batch, ldb, sb, 32, kBlockK, true);
+  }
   if (!ok) return B2G_ERR_UNSUPPORTED;
   if (pl.tma_store) {
     // C boxes of 32 x 32 fp32, 128-byte swizzled like the epilogue's staging.
@@ -470,7 +503,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     return launch_majors<128, 3, true, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
   if (pl.cluster_ctas == 2) {
     if (pl.block_n == 256)
-      return launch_majors<256, 6, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+      return launch_majors<256, B2G_PAIR256_STAGES, false, false, true>(a_mn, b_mn, ma, mb, mc, p,
+                                                                         grid, stream);
     return launch_majors<128, 8, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
   }
   if (pl.block_n == 256) {

@@ -58,6 +58,7 @@ struct EngineParams {
   int atomic_out;              // split-K: accumulate into a cleared C
   int vec_ok;                  // C rows 16-byte aligned (direct-store path)
   int tma_store;               // write C with TMA tensor stores (reduce-add for split-K)
+  int a_grouped, b_grouped;    // MN-major operand loaded as one 4-D box per stage
   int* err;
 };
 
@@ -394,6 +395,10 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
             ok = false;
             break;
           }
+#ifdef B2G_EXP_NO_LOADS
+          if (!PAIR || leader) ptx::mbar_arrive(&full[s]);
+          continue;
+#endif
           if (!PAIR)
             ptx::mbar_arrive_expect_tx(&full[s], Cfg::kStageTx);
           else if (leader)
@@ -407,8 +412,17 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
             else
               ptx::tma_load_3d(dst, map, &full[s], c0, c1, c2);
           };
+          // MN-major operand as {32, K, group, batch}: one box of all groups.
+          auto load_grouped = [&](void* dst, const CUtensorMap* map, int g0, int c3) {
+            if (PAIR)
+              ptx::tma_load_4d_pair(dst, map, full_leader + s * 8, 0, k0, g0, c3);
+            else
+              ptx::tma_load_4d(dst, map, &full[s], 0, k0, g0, c3);
+          };
           if (!A_MN) {
             load(sa, &map_a, k0, m_cta, ab);
+          } else if (p.a_grouped) {
+            load_grouped(sa, &map_a, m_cta / 32, ab);
           } else {
 #pragma unroll
             for (int j = 0; j < kBlockM / 32; ++j)
@@ -416,6 +430,8 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           }
           if (!B_MN) {
             load(sb, &map_b, k0, n_cta, bb);
+          } else if (p.b_grouped) {
+            load_grouped(sb, &map_b, n_cta / 32, bb);
           } else {
 #pragma unroll
             for (int j = 0; j < Cfg::kBnCta / 32; ++j)
@@ -558,7 +574,9 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
             ptx::tmem_ld_32x32b_x32(taddr + (ch + 2) * 32, rb);   // in flight while ra drains
           else
             release();                                            // every TMEM read is done
+#ifndef B2G_EXP_NO_STORES
           store_chunk(p, &map_c, stg, ra, u.b, row0, n0 + ch * 32, lane);
+#endif
           if (more) {
             tmem_ld_wait_regs(rb);
 #pragma unroll
