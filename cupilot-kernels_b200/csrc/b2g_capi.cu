@@ -331,12 +331,16 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
     // unit (tile width x K blocks of its split), divided by the per-SM
     // efficiency of the tile shape.  Efficiencies are measured throughputs
     // on B200 relative to the CTA-pair 256 x 256 unit (8192 x 8192 x 4096:
-    // 712 / 590 / 474 / 452 TFLOP/s): wider units stream fewer operand
-    // bytes from L2 per flop, which is what bounds these kernels, so narrow
-    // tiles rarely pay even when they fill more SMs.
-    struct Cand { int ctas, bn; double eff; };
-    const Cand cands[] = {{2, 256, 1.0}, {1, 256, 0.83}, {2, 128, 0.66}, {1, 128, 0.63}};
-    // B2G_TILE=pair256|pair128|single256|single128 pins the choice (tuning aid).
+    // 712 / 590 / 474 / 452 TFLOP/s for pair256 / single256 / pair128 /
+    // single128): wider units stream fewer operand bytes per flop through
+    // L2 and shared memory, which costs power and so clock under the 1 kW
+    // cap.  The 512-wide pair unit (no accumulator double buffering) pays
+    // off only when a unit's K loop is long enough to hide its epilogue.
+    struct Cand { int ctas, bn; double eff, eff_long_k; };
+    const Cand cands[] = {{2, 256, 1.0, 1.0}, {2, 512, 0.85, 1.05}, {1, 256, 0.83, 0.83},
+                          {2, 128, 0.66, 0.66}, {1, 128, 0.63, 0.63}};
+    // B2G_TILE=pair512|pair256|pair128|single256|single128 pins the choice
+    // (a tuning and test aid).
     static const char* forced = std::getenv("B2G_TILE");
     double best = 0.0;
     for (const Cand& c : cands) {
@@ -349,7 +353,8 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
       int64_t splits, kbps;
       choose_splits(d, units * c.ctas, kb_total, num_sms, &splits, &kbps);
       const double waves = static_cast<double>(cdiv(units * splits * c.ctas, num_sms));
-      const double cost = waves * c.bn * static_cast<double>(std::max<int64_t>(kbps, 1)) / c.eff;
+      const double eff = kbps >= 64 ? c.eff_long_k : c.eff;
+      const double cost = waves * c.bn * static_cast<double>(std::max<int64_t>(kbps, 1)) / eff;
       if (best == 0.0 || cost < best * 0.999) {
         best = cost;
         bn = c.bn;
@@ -364,7 +369,7 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   if (x3)
     pl->stages = 3;
   else if (ctas == 2)
-    pl->stages = bn == 256 ? 6 : 8;
+    pl->stages = bn == 512 ? 4 : (bn == 256 ? 6 : 8);
   else
     pl->stages = bn == 256 ? 4 : 6;
   pl->tiles_m = static_cast<int32_t>(cdiv(d->m, pl->block_m));
@@ -470,7 +475,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   }
 
   CUtensorMap ma, mb, mc;
-  const int bn_cta = pl.block_n / pl.cluster_ctas;
+  // B box: one N=256 MMA sub-tile's share per CTA (the whole tile for one CTA).
+  const int bn_cta = std::min(pl.block_n, 256) / pl.cluster_ctas;
   const int64_t k_ext = std::max<int64_t>(d->k, 1);
   bool ok;
   if (!pl.a_mn_major) {
@@ -502,6 +508,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   if (x3)
     return launch_majors<128, 3, true, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
   if (pl.cluster_ctas == 2) {
+    if (pl.block_n == 512)
+      return launch_majors<512, 4, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
     if (pl.block_n == 256)
       return launch_majors<256, B2G_PAIR256_STAGES, false, false, true>(a_mn, b_mn, ma, mb, mc, p,
                                                                          grid, stream);

@@ -115,14 +115,22 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
 }
 
 // PAIR: a cluster of two CTAs computes one 256 x BN unit with
-// tcgen05.mma.cta_group::2; each CTA holds 128 rows of A, BN/2 columns of B
-// and its 128 x BN half of the accumulator.
+// tcgen05.mma.cta_group::2; each CTA holds 128 rows of A, its half of every
+// N=256 B sub-tile and its 128 x BN part of the accumulator.  BN = 512 (pair
+// only) issues two N=256 MMAs per K step over one shared A tile: more flops
+// per operand byte streamed from L2, at the price of a single-buffered
+// accumulator (512 TMEM columns), so its epilogue does not overlap the next
+// unit's mainloop.
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR>
 struct EngineCfg {
   static constexpr int kCtas = PAIR ? 2 : 1;
   static constexpr int kUnitM = kBlockM * kCtas;
-  static constexpr int kBnCta = BN / kCtas;                 // B columns loaded per CTA
+  static constexpr int kMmaN = BN > 256 ? 256 : BN;           // N of one MMA instruction
+  static constexpr int kNSub = BN / kMmaN;                    // MMAs per K=8 step
+  static constexpr int kSubCols = kMmaN / kCtas;              // B columns per CTA per sub-tile
+  static constexpr int kBnCta = BN / kCtas;                   // B columns loaded per CTA
   static constexpr int kABytes = kBlockM * kBlockK * 4;
+  static constexpr int kBSubBytes = kSubCols * kBlockK * 4;
   static constexpr int kBBytes = kBnCta * kBlockK * 4;
   static constexpr int kStageTx = kABytes + kBBytes;        // bytes per CTA per stage
   static constexpr int kOperandBufs = X3 ? 2 : 1;
@@ -138,12 +146,13 @@ struct EngineCfg {
   static constexpr int kNumBars = 3 * STAGES + 4;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
-  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kAccBufs = BN > 256 ? 1 : 2;         // accumulator buffers in TMEM
+  static constexpr int kTmemCols = kAccBufs * BN;
   static constexpr int kXformWarps = XF ? 4 : 0;
   static constexpr int kThreads = (2 + kEpiWarps + kXformWarps) * 32;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
-  static_assert(BN % 64 == 0 && BN <= 256, "BN");
+  static_assert(BN % 64 == 0 && BN <= (PAIR ? 512 : 256), "BN");
   static_assert(!X3 || XF, "the 3xTF32 split runs in the transform warps");
   static_assert(!(PAIR && XF), "transform warps run in single-CTA units only");
 };
@@ -384,7 +393,8 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       for (long long w = unit0; w < p.work_units && ok; w += unit_step) {
         const WorkUnit u = decode_unit(p, w);
         const int m_cta = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM;
-        const int n_cta = u.tn * BN + static_cast<int>(rank) * Cfg::kBnCta;
+        // B sub-tile j of this CTA: columns [n0 + j*kMmaN + rank*kSubCols, +kSubCols)
+        const int n_cta = u.tn * BN + static_cast<int>(rank) * Cfg::kSubCols;
         const int ab = p.a_batched ? u.b : 0;
         const int bb = p.b_batched ? u.b : 0;
         for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
@@ -428,14 +438,19 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
             for (int j = 0; j < kBlockM / 32; ++j)
               load(sa + j * kBlockK * kSwRowBytes, &map_a, m_cta + 32 * j, k0, ab);
           }
-          if (!B_MN) {
-            load(sb, &map_b, k0, n_cta, bb);
-          } else if (p.b_grouped) {
-            load_grouped(sb, &map_b, n_cta / 32, bb);
-          } else {
 #pragma unroll
-            for (int j = 0; j < Cfg::kBnCta / 32; ++j)
-              load(sb + j * kBlockK * kSwRowBytes, &map_b, n_cta + 32 * j, k0, bb);
+          for (int j = 0; j < Cfg::kNSub; ++j) {
+            uint8_t* sbj = sb + j * Cfg::kBSubBytes;
+            const int nj = n_cta + j * Cfg::kMmaN;
+            if (!B_MN) {
+              load(sbj, &map_b, k0, nj, bb);
+            } else if (p.b_grouped) {
+              load_grouped(sbj, &map_b, nj / 32, bb);
+            } else {
+#pragma unroll
+              for (int g = 0; g < Cfg::kSubCols / 32; ++g)
+                load(sbj + g * kBlockK * kSwRowBytes, &map_b, nj + 32 * g, k0, bb);
+            }
           }
         }
       }
@@ -443,7 +458,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = ptx::idesc_tf32(Cfg::kUnitM, BN, A_MN, B_MN);
+      constexpr uint32_t idesc = ptx::idesc_tf32(Cfg::kUnitM, Cfg::kMmaN, A_MN, B_MN);
       // Canonical layouts (byte offsets).  K-major (128-byte swizzle): rows
       // 128 B apart, 8-row atoms 1024 B apart (SBO), LBO unused; a K=8 step
       // advances 32 B inside the row.  MN-major (32-byte-atom swizzle):
@@ -462,8 +477,8 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       for (long long w = unit0; w < p.work_units && ok; w += unit_step) {
         const WorkUnit u = decode_unit(p, w);
         if (u.kb_lo >= u.kb_hi) continue;
-        const int buf = tl & 1;
-        const uint32_t uph = (tl >> 1) & 1;
+        const int buf = tl % Cfg::kAccBufs;
+        const uint32_t uph = (tl / Cfg::kAccBufs) & 1;
         if (!ptx::mbar_wait(&tmem_empty[buf], uph ^ 1, abort_flag, kWaitLimitNs)) {
           record_error(p.err, abort_flag, kErrWaitTmemEmpty);
           break;
@@ -489,6 +504,15 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           for (int k8 = 0; k8 < kBlockK / 8; ++k8) {
             const uint64_t da = ptx::smem_desc(sa + k8 * a_kstep, a_lbo, a_sbo, a_lay);
             const uint64_t db = ptx::smem_desc(sb + k8 * b_kstep, b_lbo, b_sbo, b_lay);
+#pragma unroll
+            for (int j = 1; j < Cfg::kNSub; ++j) {
+              const uint64_t dbj =
+                  ptx::smem_desc(sb + j * Cfg::kBSubBytes + k8 * b_kstep, b_lbo, b_sbo, b_lay);
+              if (PAIR)
+                ptx::mma_tf32_pair(d_tmem + j * Cfg::kMmaN, da, dbj, idesc, acc);
+              else
+                ptx::mma_tf32(d_tmem + j * Cfg::kMmaN, da, dbj, idesc, acc);
+            }
             if (PAIR)
               ptx::mma_tf32_pair(d_tmem, da, db, idesc, acc);
             else
@@ -543,8 +567,8 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
         }
         continue;
       }
-      const int buf = tl & 1;
-      const uint32_t uph = (tl >> 1) & 1;
+      const int buf = tl % Cfg::kAccBufs;
+      const uint32_t uph = (tl / Cfg::kAccBufs) & 1;
       if (!ptx::mbar_wait(&tmem_full[buf], uph, abort_flag, kWaitLimitNs)) {
         if (lane == 0) record_error(p.err, abort_flag, kErrWaitTmemFull);
         break;
