@@ -407,6 +407,9 @@ def main():
         line["impl"] = "reference"
         line["reference"] = ("kernels/3_Batched_matrix_multiplication_best_kernel.cu:113 "
                              "batched_matmul_cuda, compiled unmodified for sm_100a")
+    if args.impl == "ours" and not args.no_shapes:
+        line["large_k_split"] = large_k_split(W, peaks, world, rank, min(args.steps, 100),
+                                              args.warmup)
     if rank == 0 and world == 1 and args.impl == "ours" and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(w)
     if rank == 0 and world == 1 and args.impl == "ours" and not args.no_shapes:
@@ -451,6 +454,29 @@ def end_to_end(args, w, A, B, op, world):
            "d2h_bytes_per_step": s["batch"] * s["m"] * s["n"] * 4}
     return e2e
 
+
+
+def large_k_split(W, peaks, world, rank, steps, warmup):
+    """Large-K config with K split across the ranks (strong scaling: total K
+    fixed) and the 256x256 partials summed by one NCCL reduce to rank 0."""
+    part = _pkg("partition").Partitioner.from_env()
+    w = W["large_k"]
+    m, n, k = w.shapes["m"], w.shapes["n"], w.shapes["k"]
+    k0, k1 = part.k_range(k)
+    g = torch.Generator(device="cuda").manual_seed(7000 + rank)
+    A = torch.randn(m, k1 - k0, generator=g, device="cuda")
+    B = torch.randn(k1 - k0, n, generator=g, device="cuda")
+    fn = lambda: part.split_k_matmul(A, B, root=0)
+    total, _ = time_loop(fn, steps, warmup, world, per_launch=False)
+    ms = total / steps
+    return {"workload": "large_k (BASELINE configs[3]; reference PID 6)", "k_total": k,
+            "k_per_rank": k1 - k0, "ms": round(ms, 4),
+            "gbs": round(w.min_bytes / (ms / 1e3) / 1e9, 1),
+            "tflops": round(w.flops / (ms / 1e3) / 1e12, 2),
+            "frac_hbm_1gpu": round(w.min_bytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"], 3),
+            "collective": "local split-K GEMM, then NCCL reduce of the 256 KB partial to rank 0"
+                          if world > 1 else "none (one GPU)",
+            "scaling": "strong"}
 
 
 def shape_table(W, peaks, only, ops):

@@ -1,0 +1,144 @@
+"""Single-box partitioner: one process per GPU, torch.distributed for plumbing.
+
+Two ways to spread one operator call over the GPUs of a node:
+
+* Batch / M sharding (batched, 3-D and 4-D products, any plain GEMM along M):
+  rank r owns a contiguous, balanced slice of the batch (or of M) and
+  computes it with the local kernel.  No communication: outputs stay sharded
+  (`gather_rows` brings them together when a caller wants one tensor).
+* K splitting (large-K, reference kernels/6_Matmul_with_large_K_dimension_best_kernel.cu,
+  whose 8 streams + 7 `C.add_` on one GPU at K6:147-200 become ranks +
+  a reduction): rank r multiplies A[:, K_r] by B[K_r, :] locally, then the
+  partial products are summed by one NCCL reduce over NVLink to the root
+  (or an all-reduce when every rank needs C).
+
+The local product is the package's own GEMM (`ops`); callers may inject a
+different `local_matmul` (the host-side tests run the orchestration on CPU
+ranks with gloo).  Every collective runs under the process group's timeout,
+so a rank that dies or stalls surfaces as an error on the others instead of
+a hang.
+"""
+from __future__ import annotations
+
+import datetime
+from dataclasses import dataclass
+from typing import Callable, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(total: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous [start, stop) of `total` items owned by `rank`; the first
+    total % world ranks get one extra item."""
+    if world <= 0 or not 0 <= rank < world or total < 0:
+        raise ValueError(f"bad shard request total={total} world={world} rank={rank}")
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    stop = start + base + (1 if rank < extra else 0)
+    return start, stop
+
+
+def shard_plan(total: int, world: int) -> List[Tuple[int, int]]:
+    return [shard_range(total, world, r) for r in range(world)]
+
+
+def k_split_plan(k: int, world: int, align: int = 32) -> List[Tuple[int, int]]:
+    """K ranges per rank, rounded to `align` (the kernel's K block) so no
+    rank's slice straddles a K block except the last; every range may be
+    empty only when k < world * align."""
+    blocks = (k + align - 1) // align
+    out = []
+    for r in range(world):
+        b0, b1 = shard_range(blocks, world, r)
+        out.append((min(b0 * align, k), min(b1 * align, k)))
+    return out
+
+
+def _default_matmul():
+    import importlib
+
+    ops = importlib.import_module(__package__ + ".ops")
+    return lambda A, B: ops.gemm(A, B, False, False, 0)
+
+
+@dataclass
+class Partitioner:
+    """Per-rank view of the node: rank, world size and the process group."""
+
+    rank: int
+    world: int
+    group: Optional[dist.ProcessGroup] = None
+    local_matmul: Optional[Callable] = None
+
+    @classmethod
+    def from_env(cls, local_matmul: Optional[Callable] = None, group=None) -> "Partitioner":
+        if dist.is_available() and dist.is_initialized():
+            return cls(dist.get_rank(group), dist.get_world_size(group), group, local_matmul)
+        return cls(0, 1, None, local_matmul)
+
+    def _mm(self):
+        if self.local_matmul is None:
+            self.local_matmul = _default_matmul()
+        return self.local_matmul
+
+    # ------------------------------------------------------------ sharding
+    def batch_range(self, batch: int) -> Tuple[int, int]:
+        return shard_range(batch, self.world, self.rank)
+
+    def batched_matmul_shard(self, A_shard: torch.Tensor, B_shard: torch.Tensor,
+                             bmm: Optional[Callable] = None) -> torch.Tensor:
+        """C[b] = A[b] B[b] for this rank's batch slice (no communication)."""
+        if bmm is None:
+            import importlib
+
+            bmm = importlib.import_module(__package__ + ".ops").p3.forward
+        return bmm(A_shard, B_shard)
+
+    def gather_rows(self, local: torch.Tensor, total_rows: int) -> torch.Tensor:
+        """All-gather row shards (of shard_plan sizes) into one tensor on every rank."""
+        if self.world == 1:
+            return local
+        plan = shard_plan(total_rows, self.world)
+        width = max(b - a for a, b in plan)
+        pad = torch.zeros((width,) + tuple(local.shape[1:]), dtype=local.dtype,
+                          device=local.device)
+        pad[: local.shape[0]] = local
+        bufs = [torch.empty_like(pad) for _ in range(self.world)]
+        dist.all_gather(bufs, pad, group=self.group)
+        return torch.cat([bufs[r][: b - a] for r, (a, b) in enumerate(plan)], dim=0)
+
+    # ------------------------------------------------------------ K splitting
+    def k_range(self, k: int) -> Tuple[int, int]:
+        return k_split_plan(k, self.world)[self.rank]
+
+    def split_k_matmul(self, A_k: torch.Tensor, B_k: torch.Tensor, root: int = 0,
+                       all_ranks: bool = False) -> Optional[torch.Tensor]:
+        """Given this rank's K slice (A[:, K_r], B[K_r, :]), return C = A B on
+        the root (None elsewhere), or on every rank when all_ranks."""
+        if A_k.shape[1] == 0:
+            part = torch.zeros(A_k.shape[0], B_k.shape[1], dtype=A_k.dtype, device=A_k.device)
+        else:
+            part = self._mm()(A_k, B_k)
+        if self.world == 1:
+            return part
+        if all_ranks:
+            dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+            return part
+        dist.reduce(part, dst=root, op=dist.ReduceOp.SUM, group=self.group)
+        return part if self.rank == root else None
+
+
+def init_node(backend: str = "nccl", timeout_s: float = 60.0) -> Partitioner:
+    """Join the node's process group from torchrun's environment (RANK,
+    WORLD_SIZE, LOCAL_RANK, MASTER_ADDR/PORT) with a bounded timeout."""
+    import os
+
+    if not dist.is_initialized():
+        kw = dict(backend=backend, timeout=datetime.timedelta(seconds=timeout_s))
+        if backend == "nccl":
+            local = int(os.environ.get("LOCAL_RANK", "0"))
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(**kw)
+    return Partitioner.from_env()
