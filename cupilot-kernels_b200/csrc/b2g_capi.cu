@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -56,6 +57,33 @@ int device_state(DeviceState** out) {
   }
   *out = &st;
   return B2G_OK;
+}
+
+// ---------------------------------------------------------------- fault-detection knobs
+// B2G_WAIT_LIMIT_MS bounds every device-side wait (default 2000 ms).
+// B2G_TEST_STALL_ONCE=1 is a test hook: the first GEMM launched in the
+// process withholds its "accumulator ready" signal, so the epilogue's bounded
+// wait runs out, the kernel records kErrWaitTmemFull in the device error
+// word and unwinds; later launches are normal.  Nothing faults or traps.
+long long wait_limit_ns() {
+  static const long long ns = [] {
+    const char* e = std::getenv("B2G_WAIT_LIMIT_MS");
+    const long long ms = (e && *e) ? std::atoll(e) : 0;
+    return ms > 0 ? ms * 1000000ll : static_cast<long long>(kWaitLimitNs);
+  }();
+  return ns;
+}
+
+int take_injected_stall() {
+  static std::atomic<int> armed{-1};
+  int v = armed.load();
+  if (v < 0) {
+    const char* e = std::getenv("B2G_TEST_STALL_ONCE");
+    int want = (e && *e == '1') ? 1 : 0;
+    armed.compare_exchange_strong(v, want);
+  }
+  int one = 1;
+  return armed.compare_exchange_strong(one, 0) ? 1 : 0;
 }
 
 // ---------------------------------------------------------------- tensor maps
@@ -463,6 +491,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.vec_ok = (reinterpret_cast<uintptr_t>(d->c) % 16 == 0) && (d->ldc % 4 == 0) &&
              (d->batch == 1 || d->stride_c % 4 == 0);
   p.tma_store = pl.tma_store;
+  p.wait_limit_ns = wait_limit_ns();
+  p.inject_stall = take_injected_stall();
   p.err = err_word;
 
   if (p.atomic_out) {

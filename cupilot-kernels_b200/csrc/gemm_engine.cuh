@@ -29,7 +29,8 @@ namespace b2g {
 constexpr int kBlockM = 128;
 constexpr int kBlockK = 32;              // fp32 elements in one 128-byte swizzle row
 constexpr int kSwRowBytes = 128;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s per wait, then give up
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // default bound on a wait: 2 s
+constexpr uint64_t kDrainLimitNs = 100000000ull;   // 0.1 s for in-flight loads at exit
 
 enum : int { kTriNone = 0, kTriUpper = 1, kTriLower = 2 };
 
@@ -59,6 +60,8 @@ struct EngineParams {
   int vec_ok;                  // C rows 16-byte aligned (direct-store path)
   int tma_store;               // write C with TMA tensor stores (reduce-add for split-K)
   int a_grouped, b_grouped;    // MN-major operand loaded as one 4-D box per stage
+  long long wait_limit_ns;     // bound on every mbarrier wait
+  int inject_stall;            // test hook: the MMA warp never signals tmem_full
   int* err;
 };
 
@@ -143,7 +146,7 @@ struct EngineCfg {
   static constexpr int kEpiBufBytes = 32 * 32 * 4;           // one 32 x 32 fp32 box
   static constexpr int kEpiBytes = kEpiWarps * kEpiBufBytes;
   static constexpr int kOffBar = kOffEpi + kEpiBytes;
-  static constexpr int kNumBars = 3 * STAGES + 4;
+  static constexpr int kNumBars = 3 * STAGES + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
   static constexpr int kAccBufs = BN > 256 ? 1 : 2;         // accumulator buffers in TMEM
@@ -341,6 +344,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
   uint64_t* ready = bars + 2 * STAGES;
   uint64_t* tmem_full = bars + 3 * STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
+  uint64_t* mma_drain = tmem_full + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 4);
 
@@ -361,6 +365,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       ptx::mbar_init(&tmem_full[b], 1);
       ptx::mbar_init(&tmem_empty[b], Cfg::kEpiWarps * Cfg::kCtas);
     }
+    ptx::mbar_init(mma_drain, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -400,7 +405,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
         for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, kWaitLimitNs)) {
+          if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, p.wait_limit_ns)) {
             record_error(p.err, abort_flag, kErrWaitEmpty);
             ok = false;
             break;
@@ -454,6 +459,16 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           }
         }
       }
+      // Drain: the bytes of every stage issued must land before the CTA may
+      // exit, also when another role gave up early (bounded; a no-op on the
+      // normal path, where the MMA warp already waited for each of them).
+      // The pair leader's barriers also count the peer's loads.
+      if (!PAIR || leader) {
+        volatile int never = 0;
+        const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
+        for (uint32_t j = first; j < it; ++j)
+          ptx::mbar_wait(&full[j % STAGES], (j / STAGES) & 1, &never, kDrainLimitNs);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -479,7 +494,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
         if (u.kb_lo >= u.kb_hi) continue;
         const int buf = tl % Cfg::kAccBufs;
         const uint32_t uph = (tl / Cfg::kAccBufs) & 1;
-        if (!ptx::mbar_wait(&tmem_empty[buf], uph ^ 1, abort_flag, kWaitLimitNs)) {
+        if (!ptx::mbar_wait(&tmem_empty[buf], uph ^ 1, abort_flag, p.wait_limit_ns)) {
           record_error(p.err, abort_flag, kErrWaitTmemEmpty);
           break;
         }
@@ -490,7 +505,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           uint64_t* gate = XF ? &ready[s] : &full[s];
-          if (!ptx::mbar_wait(gate, ph, abort_flag, kWaitLimitNs)) {
+          if (!ptx::mbar_wait(gate, ph, abort_flag, p.wait_limit_ns)) {
             record_error(p.err, abort_flag, XF ? kErrWaitReady : kErrWaitFull);
             ok = false;
             break;
@@ -531,12 +546,22 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
             ptx::mma_commit(&empty[s]);
         }
         if (!ok) break;
-        if (PAIR)
-          ptx::mma_commit_pair(&tmem_full[buf], 0x3);
-        else
-          ptx::mma_commit(&tmem_full[buf]);
+        if (!p.inject_stall) {
+          if (PAIR)
+            ptx::mma_commit_pair(&tmem_full[buf], 0x3);
+          else
+            ptx::mma_commit(&tmem_full[buf]);
+        }
         ++tl;
       }
+      // Drain: no MMA may still write TMEM when the allocation is freed,
+      // also after an early exit (bounded; immediate on the normal path).
+      if (PAIR)
+        ptx::mma_commit_pair(mma_drain, 0x1);
+      else
+        ptx::mma_commit(mma_drain);
+      volatile int never = 0;
+      ptx::mbar_wait(mma_drain, 0, &never, kDrainLimitNs);
     }
   } else if (warp < 2 + Cfg::kEpiWarps) {
     // ------------------------------------------------------------ epilogue
@@ -569,7 +594,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       }
       const int buf = tl % Cfg::kAccBufs;
       const uint32_t uph = (tl / Cfg::kAccBufs) & 1;
-      if (!ptx::mbar_wait(&tmem_full[buf], uph, abort_flag, kWaitLimitNs)) {
+      if (!ptx::mbar_wait(&tmem_full[buf], uph, abort_flag, p.wait_limit_ns)) {
         if (lane == 0) record_error(p.err, abort_flag, kErrWaitTmemFull);
         break;
       }
@@ -625,7 +650,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        if (!ptx::mbar_wait(&full[s], ph, abort_flag, kWaitLimitNs)) {
+        if (!ptx::mbar_wait(&full[s], ph, abort_flag, p.wait_limit_ns)) {
           if (lane == 0) record_error(p.err, abort_flag, kErrWaitXform);
           ok = false;
           break;
