@@ -435,21 +435,30 @@ def end_to_end(args, w, A, B, op, world):
     A_d = torch.empty_like(A)
     B_d = torch.empty_like(B)
     if args.impl == "ours":
-        e2e_call = lambda: op(A_d, B_d)
+        # The package's host-buffer entry: batch chunks streamed through
+        # three CUDA streams (upload / GEMM / download overlap).
+        ops = _pkg("ops")
+
+        def e2e_step():
+            ops.batched_matmul_from_host(A_h, B_h, out=C_h, chunks=8, synchronize=False)
     else:
+        # The reference's entry point takes device tensors: copy in, call, copy out.
         e2e_call, _ = reference_callable(HEADLINE, A_d, B_d)
 
-    def e2e_step():
-        A_d.copy_(A_h, non_blocking=True)
-        B_d.copy_(B_h, non_blocking=True)
-        C = e2e_call()
-        C_h.copy_(C, non_blocking=True)
+        def e2e_step():
+            A_d.copy_(A_h, non_blocking=True)
+            B_d.copy_(B_h, non_blocking=True)
+            C = e2e_call()
+            C_h.copy_(C, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 20))
     e2e_ms, _ = time_loop(e2e_step, e2e_steps, 2, world, per_launch=False)
     e2e_per = e2e_ms / e2e_steps
     e2e = {"value": round(world * w.flops / (e2e_per / 1e3) / 1e12, 3), "unit": "TFLOP/s",
            "ms_per_step": round(e2e_per, 3),
+           "path": ("ops.batched_matmul_from_host: pinned host A, B -> C, 8 batch chunks "
+                    "pipelined over upload / GEMM / download streams") if args.impl == "ours"
+                   else "reference batched_matmul_cuda on device copies of pinned host A, B",
            "h2d_bytes_per_step": A.numel() * 4 + B.numel() * 4,
            "d2h_bytes_per_step": s["batch"] * s["m"] * s["n"] * 4}
     return e2e

@@ -23,6 +23,9 @@
 #ifndef B2G_PAIR256_STAGES
 #define B2G_PAIR256_STAGES 6   // pipeline depth of the CTA-pair 256-wide engine
 #endif
+#ifndef B2G_PAIR256_EPIG
+#define B2G_PAIR256_EPIG 1     // accumulator chunks per epilogue store group
+#endif
 
 namespace b2g {
 namespace {
@@ -213,11 +216,11 @@ __global__ void rowscale_scalar_kernel(const float* __restrict__ d, const float*
 }
 
 // ---------------------------------------------------------------- engine instantiations
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR>
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG>
 int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
                   const EngineParams& p, int grid, cudaStream_t stream) {
-  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR>;
-  auto kern = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, X3, XF, PAIR>;
+  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>;
+  auto kern = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>;
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -245,16 +248,16 @@ int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
   return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
 }
 
-template <int BN, int STAGES, bool X3, bool XF, bool PAIR>
+template <int BN, int STAGES, bool X3, bool XF, bool PAIR, int EPIG = 1>
 int launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb,
                   const CUtensorMap& mc, const EngineParams& p, int grid, cudaStream_t st) {
   if (!a_mn && !b_mn)
-    return launch_engine<BN, STAGES, false, false, X3, XF, PAIR>(ma, mb, mc, p, grid, st);
+    return launch_engine<BN, STAGES, false, false, X3, XF, PAIR, EPIG>(ma, mb, mc, p, grid, st);
   if (!a_mn && b_mn)
-    return launch_engine<BN, STAGES, false, true, X3, XF, PAIR>(ma, mb, mc, p, grid, st);
+    return launch_engine<BN, STAGES, false, true, X3, XF, PAIR, EPIG>(ma, mb, mc, p, grid, st);
   if (a_mn && !b_mn)
-    return launch_engine<BN, STAGES, true, false, X3, XF, PAIR>(ma, mb, mc, p, grid, st);
-  return launch_engine<BN, STAGES, true, true, X3, XF, PAIR>(ma, mb, mc, p, grid, st);
+    return launch_engine<BN, STAGES, true, false, X3, XF, PAIR, EPIG>(ma, mb, mc, p, grid, st);
+  return launch_engine<BN, STAGES, true, true, X3, XF, PAIR, EPIG>(ma, mb, mc, p, grid, st);
 }
 
 bool valid_desc(const b2g_gemm_desc* d) {
@@ -541,8 +544,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     if (pl.block_n == 512)
       return launch_majors<512, 4, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
     if (pl.block_n == 256)
-      return launch_majors<256, B2G_PAIR256_STAGES, false, false, true>(a_mn, b_mn, ma, mb, mc, p,
-                                                                         grid, stream);
+      return launch_majors<256, B2G_PAIR256_STAGES, false, false, true, B2G_PAIR256_EPIG>(
+          a_mn, b_mn, ma, mb, mc, p, grid, stream);
     return launch_majors<128, 8, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
   }
   if (pl.block_n == 256) {

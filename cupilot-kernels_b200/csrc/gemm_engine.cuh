@@ -124,7 +124,7 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
 // per operand byte streamed from L2, at the price of a single-buffered
 // accumulator (512 TMEM columns), so its epilogue does not overlap the next
 // unit's mainloop.
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR>
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG = 1>
 struct EngineCfg {
   static constexpr int kCtas = PAIR ? 2 : 1;
   static constexpr int kUnitM = kBlockM * kCtas;
@@ -144,7 +144,9 @@ struct EngineCfg {
   static constexpr int kOffEpi = STAGES * (kABytes + kBBytes) * kOperandBufs;
   static constexpr int kEpiWarps = 8;                        // two per TMEM lane quadrant
   static constexpr int kEpiBufBytes = 32 * 32 * 4;           // one 32 x 32 fp32 box
-  static constexpr int kEpiBytes = kEpiWarps * kEpiBufBytes;
+  static constexpr int kEpiBufs = EPIG;                      // staging boxes per epilogue warp
+  static constexpr int kEpiGroup = EPIG;                     // chunks staged per fence
+  static constexpr int kEpiBytes = kEpiWarps * kEpiBufs * kEpiBufBytes;
   static constexpr int kOffBar = kOffEpi + kEpiBytes;
   static constexpr int kNumBars = 3 * STAGES + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
@@ -274,9 +276,10 @@ __device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
 // global memory.  TMA path: swizzled 4 KB staging box -> tensor store (or
 // fp32 add-reduction for split-K); otherwise a swizzled transpose and
 // coalesced (or scalar, or atomic) stores.
+template <int NBUF>
 __device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtensorMap* map_c,
-                                            float* stg, uint32_t (&r)[32], int b, int row0,
-                                            int col0, int lane) {
+                                            float* stg, uint32_t& seq, uint32_t (&r)[32], int b,
+                                            int row0, int col0, int lane) {
   const int row = row0 + lane;
   if (p.tri == kTriUpper) {
 #pragma unroll
@@ -287,9 +290,25 @@ __device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtenso
     for (int j = 0; j < 32; ++j)
       if (col0 + j > row) r[j] = 0u;
   }
+#ifdef B2G_EXP_DIRECT_ROWS
   if (p.tma_store) {
-    float* buf = stg;
-    if (lane == 0) ptx::bulk_wait_read<0>();   // the previous store has read the buffer
+    if (row < p.M) {
+      float* crow = p.C + static_cast<long long>(b) * p.stride_c + static_cast<long long>(row) * p.ldc;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (col0 + 4 * j + 3 < p.N)
+          *reinterpret_cast<float4*>(crow + col0 + 4 * j) =
+              make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+    }
+    return;
+  }
+#endif
+  if (p.tma_store) {
+    // NBUF staging boxes per warp: wait until the store issued from this
+    // box NBUF chunks ago has read it (up to NBUF - 1 stay in flight).
+    float* buf = stg + (seq % NBUF) * (32 * 32);
+    if (lane == 0) ptx::bulk_wait_read<NBUF - 1>();
     __syncwarp();
 #pragma unroll
     for (int j = 0; j < 8; ++j)
@@ -305,6 +324,7 @@ __device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtenso
         ptx::tma_store_3d(map_c, buf, col0, row0, b);
       ptx::bulk_commit();
     }
+    ++seq;
     return;
   }
   float* cb = p.C + static_cast<long long>(b) * p.stride_c;
@@ -328,12 +348,59 @@ __device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtenso
   __syncwarp();
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR>
-__global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR>::kThreads, 1)
+// G accumulator chunks of a warp (row = lane; chunk g at column col0[g]) to
+// global memory through G swizzled staging boxes: one wait for the previous
+// group's stores to have read the boxes, one proxy fence, G tensor stores
+// (or fp32 add-reductions for split-K).
+template <int G>
+__device__ __forceinline__ void store_group_tma(const EngineParams& p, const CUtensorMap* map_c,
+                                                float* stg, uint32_t (&r)[G][32], int ng, int b,
+                                                int row0, const int (&col0)[G], int lane) {
+  const int row = row0 + lane;
+  if (p.tri != kTriNone) {
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int col = col0[g] + j;
+        if (p.tri == kTriUpper ? (col < row) : (col > row)) r[g][j] = 0u;
+      }
+  }
+  if (lane == 0) ptx::bulk_wait_read<0>();
+  __syncwarp();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (g < ng) {
+      float* buf = stg + g * 32 * 32;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(buf + lane * 32 + ((j ^ (lane & 7)) * 4)) =
+            make_float4(__uint_as_float(r[g][4 * j]), __uint_as_float(r[g][4 * j + 1]),
+                        __uint_as_float(r[g][4 * j + 2]), __uint_as_float(r[g][4 * j + 3]));
+    }
+  }
+  ptx::fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      if (g < ng) {
+        if (p.atomic_out)
+          ptx::tma_reduce_add_3d(map_c, stg + g * 32 * 32, col0[g], row0, b);
+        else
+          ptx::tma_store_3d(map_c, stg + g * 32 * 32, col0[g], row0, b);
+      }
+    }
+    ptx::bulk_commit();
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG>
+__global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>::kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_b,
                      const __grid_constant__ CUtensorMap map_c, const EngineParams p) {
-  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR>;
+  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -570,10 +637,10 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
     const int quad = warp & 3;
     const int ew = warp - 2;
     const int half = ew >> 2;
-    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffEpi) + ew * 32 * 32;
+    float* stg = reinterpret_cast<float*>(smem + Cfg::kOffEpi) + ew * Cfg::kEpiBufs * 32 * 32;
     const uint32_t tmem_empty_leader =
         PAIR ? ptx::mapa_shared(ptx::smem_addr(tmem_empty), 0) : 0u;
-    uint32_t tl = 0;
+    uint32_t tl = 0, seq = 0;
     for (long long w = unit0; w < p.work_units; w += unit_step) {
       const WorkUnit u = decode_unit(p, w);
       const int row0 = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM + quad * 32;
@@ -611,7 +678,31 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       };
       int nch = (p.N - n0 + 31) / 32;
       if (nch > BN / 32) nch = BN / 32;
-      if (row0 < p.M && half < nch) {
+      if (row0 < p.M && half < nch && p.tma_store) {
+        // TMA path: groups of kEpiGroup chunks, one TMEM wait and one fence each.
+        constexpr int G = Cfg::kEpiGroup;
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
+        const int mine = (nch - half + 1) / 2;                 // chunks half, half+2, ...
+#pragma unroll 1
+        for (int g0 = 0; g0 < mine; g0 += G) {
+          const int ng = mine - g0 < G ? mine - g0 : G;
+          uint32_t r[G][32];
+          int col0[G];
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const int ch = half + 2 * (g0 + (g < ng ? g : 0));
+            col0[g] = n0 + ch * 32;
+            if (g < ng) ptx::tmem_ld_32x32b_x32(taddr + ch * 32, r[g]);
+          }
+          ptx::tmem_ld_wait();
+#pragma unroll
+          for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[g][i]));
+          if (g0 + G >= mine) release();                      // every TMEM read is done
+          store_group_tma<G>(p, &map_c, stg, r, ng, u.b, row0, col0, lane);
+        }
+      } else if (row0 < p.M && half < nch) {
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
         uint32_t ra[32], rb[32];
         ptx::tmem_ld_32x32b_x32(taddr + half * 32, ra);
@@ -624,7 +715,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           else
             release();                                            // every TMEM read is done
 #ifndef B2G_EXP_NO_STORES
-          store_chunk(p, &map_c, stg, ra, u.b, row0, n0 + ch * 32, lane);
+          store_chunk<Cfg::kEpiBufs>(p, &map_c, stg, seq, ra, u.b, row0, n0 + ch * 32, lane);
 #endif
           if (more) {
             tmem_ld_wait_regs(rb);
@@ -637,7 +728,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       }
       ++tl;
     }
-    if (lane == 0) ptx::bulk_wait_all();
+    if (lane == 0) ptx::bulk_wait_read<0>();   // staging boxes read before the CTA exits
   } else if (XF) {
     // ------------------------------------------------------------ transform
     const int xt = threadIdx.x - (2 + Cfg::kEpiWarps) * 32;

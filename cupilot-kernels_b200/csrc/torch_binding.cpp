@@ -155,19 +155,28 @@ at::Tensor lower_tri_matmul(at::Tensor A, at::Tensor B) {
   return matmul_2d(A, B, B2G_OP_TRI_LOWER);
 }
 
-// kernels/3_Batched_matrix_multiplication_best_kernel.cu:113 — C[b] = A[b] B[b]
-at::Tensor batched_matmul(at::Tensor A, at::Tensor B) {
+// C[b] = A[b] B[b] into a caller-provided C (batch, M, N), row-major.
+void batched_matmul_into(const at::Tensor& A, const at::Tensor& B, at::Tensor& C) {
   check_input(A, "A");
   check_input(B, "B");
+  check_input(C, "C");
   TORCH_CHECK(A.dim() == 3 && B.dim() == 3, "A and B must be 3-D");
   TORCH_CHECK(A.size(0) == B.size(0) && A.size(2) == B.size(1), "bmm shape mismatch: ",
               A.sizes(), " x ", B.sizes());
-  TORCH_CHECK(A.device() == B.device(), "A and B must be on the same device");
-  const c10::cuda::CUDAGuard guard(A.device());
+  TORCH_CHECK(A.device() == B.device() && A.device() == C.device(),
+              "A, B and C must be on the same device");
   const int64_t bs = A.size(0), M = A.size(1), K = A.size(2), N = B.size(2);
-  at::Tensor C = at::empty({bs, M, N}, A.options());
-  if (bs == 0 || M == 0 || N == 0) return C;
-  if (K == 0) return C.zero_();
+  TORCH_CHECK(C.dim() == 3 && C.size(0) == bs && C.size(1) == M && C.size(2) == N,
+              "C must be (batch, M, N)");
+  TORCH_CHECK(C.stride(2) == 1 && C.stride(1) >= std::max<int64_t>(N, 1) &&
+                  (bs == 1 || C.stride(0) >= M * C.stride(1)),
+              "C must be row-major per batch");
+  const c10::cuda::CUDAGuard guard(A.device());
+  if (bs == 0 || M == 0 || N == 0) return;
+  if (K == 0) {
+    C.zero_();
+    return;
+  }
   at::Tensor a = A.stride(2) == 1 ? A : A.contiguous();
   at::Tensor b = B.stride(2) == 1 ? B : B.contiguous();
   TORCH_CHECK(bs <= 65535, "batch too large");
@@ -185,11 +194,21 @@ at::Tensor batched_matmul(at::Tensor A, at::Tensor B) {
   d.ldb = std::max<int64_t>(b.stride(1), N);
   d.stride_b = bs > 1 ? b.stride(0) : 0;
   d.c = C.data_ptr<float>();
-  d.ldc = N;
-  d.stride_c = M * N;
+  d.ldc = C.stride(1);
+  d.stride_c = bs > 1 ? C.stride(0) : 0;
   run_gemm(d, A);
+}
+
+// kernels/3_Batched_matrix_multiplication_best_kernel.cu:113 — C[b] = A[b] B[b]
+at::Tensor batched_matmul(at::Tensor A, at::Tensor B) {
+  check_input(A, "A");
+  TORCH_CHECK(A.dim() == 3 && B.dim() == 3, "A and B must be 3-D");
+  at::Tensor C = at::empty({A.size(0), A.size(1), B.size(2)}, A.options());
+  batched_matmul_into(A, B, C);
   return C;
 }
+
+void batched_matmul_out(at::Tensor A, at::Tensor B, at::Tensor C) { batched_matmul_into(A, B, C); }
 
 // kernels/10_3D_tensor_matrix_multiplication_best_kernel.cu:180 — out[n] = A[n] B,
 // A (n, m, k), B (k, l): the batch folds into M (B is shared).
@@ -256,6 +275,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("square_matmul", &square_matmul);
   m.def("standard_matmul", &standard_matmul);
   m.def("batched_matmul", &batched_matmul);
+  m.def("batched_matmul_out", &batched_matmul_out, "C[b] = A[b] B[b] into a preallocated C");
   m.def("large_k_matmul", &large_k_matmul);
   m.def("small_k_matmul", &small_k_matmul);
   m.def("irregular_matmul", &irregular_matmul);

@@ -124,3 +124,82 @@ for _pid, _op in OPERATORS.items():
 
 gemm = _ext.gemm
 read_device_error = _ext.read_device_error
+
+
+batched_matmul_out = _ext.batched_matmul_out
+
+_HOST_STREAMS = {}
+
+
+def _host_streams(device):
+    key = torch_device_index(device)
+    if key not in _HOST_STREAMS:
+        import torch
+
+        with torch.cuda.device(key):
+            _HOST_STREAMS[key] = (torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream())
+    return _HOST_STREAMS[key]
+
+
+def torch_device_index(device):
+    import torch
+
+    d = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    return d.index if d.index is not None else torch.cuda.current_device()
+
+
+def batched_matmul_from_host(A_h, B_h, out=None, chunks=8, device=None, synchronize=True):
+    """C = A @ B (batched, fp32) for host tensors, streamed through one GPU.
+
+    The batch is cut into `chunks` pieces; on three CUDA streams the upload
+    of piece i+1, the GEMM of piece i and the download of piece i-1 run at
+    the same time, so PCIe is busy in both directions while the tensor cores
+    work.  A_h (batch, M, K) and B_h (batch, K, N) should be pinned for the
+    copies to be asynchronous; `out` (batch, M, N), pinned host memory, is
+    allocated when not given.  The caller's current stream is made to wait
+    for the last download; with synchronize=True (default) the call also
+    blocks until `out` holds the result, otherwise synchronise the current
+    stream before reading `out`.
+    """
+    import torch
+
+    if A_h.dim() != 3 or B_h.dim() != 3 or A_h.shape[0] != B_h.shape[0] \
+            or A_h.shape[2] != B_h.shape[1]:
+        raise ValueError(f"bmm shape mismatch: {tuple(A_h.shape)} x {tuple(B_h.shape)}")
+    if A_h.dtype != torch.float32 or B_h.dtype != torch.float32:
+        raise TypeError("A and B must be float32")
+    bs, M, K = A_h.shape
+    N = B_h.shape[2]
+    dev = torch.device("cuda", torch_device_index(device))
+    if out is None:
+        out = torch.empty(bs, M, N, dtype=torch.float32, pin_memory=True)
+    if bs == 0:
+        return out
+    s_in, s_mm, s_out = _host_streams(dev)
+    A_d = torch.empty(bs, M, K, dtype=torch.float32, device=dev)
+    B_d = torch.empty(bs, K, N, dtype=torch.float32, device=dev)
+    C_d = torch.empty(bs, M, N, dtype=torch.float32, device=dev)
+    step = max(1, (bs + chunks - 1) // chunks)
+    pieces = [(b0, min(bs, b0 + step)) for b0 in range(0, bs, step)]
+    cur = torch.cuda.current_stream(dev)
+    for s in (s_in, s_mm, s_out):
+        s.wait_stream(cur)
+    for b0, b1 in pieces:
+        with torch.cuda.stream(s_in):
+            A_d[b0:b1].copy_(A_h[b0:b1], non_blocking=True)
+            B_d[b0:b1].copy_(B_h[b0:b1], non_blocking=True)
+        s_mm.wait_stream(s_in)
+        with torch.cuda.stream(s_mm):
+            batched_matmul_out(A_d[b0:b1], B_d[b0:b1], C_d[b0:b1])
+        s_out.wait_stream(s_mm)
+        with torch.cuda.stream(s_out):
+            out[b0:b1].copy_(C_d[b0:b1], non_blocking=True)
+    for t in (A_d, B_d):
+        t.record_stream(s_in)
+        t.record_stream(s_mm)
+    C_d.record_stream(s_mm)
+    C_d.record_stream(s_out)
+    cur.wait_stream(s_out)
+    if synchronize:
+        s_out.synchronize()
+    return out

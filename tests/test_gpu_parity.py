@@ -230,3 +230,22 @@ def test_capi_direct_call(capi):
 def test_no_device_errors_recorded(ops):
     torch.cuda.synchronize()
     assert ops.read_device_error(torch.cuda.current_device()) == 0
+
+
+@pytest.mark.parametrize("chunks", [1, 3, 8])
+def test_batched_matmul_from_host_streams_chunks(ops, chunks):
+    g = _gen(77 + chunks)
+    A = _randn(g, 10, 130, 96).pin_memory()
+    B = _randn(g, 10, 96, 200).pin_memory()
+    C = ops.batched_matmul_from_host(A, B, chunks=chunks)
+    assert C.shape == (10, 130, 200) and not C.is_cuda
+    _check(C, O.batched(A.numpy(), B.numpy()), "tf32")
+    ref = ops.p3.forward(A.cuda(), B.cuda()).cpu()
+    assert torch.equal(C, ref)
+
+
+def test_batched_matmul_out_validates_shapes(ops):
+    A = torch.randn(2, 8, 4, device="cuda")
+    B = torch.randn(2, 4, 6, device="cuda")
+    with pytest.raises(RuntimeError, match="C must be"):
+        ops.batched_matmul_out(A, B, torch.empty(2, 8, 5, device="cuda"))
