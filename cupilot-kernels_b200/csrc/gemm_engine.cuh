@@ -661,7 +661,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       }
       const int buf = tl % Cfg::kAccBufs;
       const uint32_t uph = (tl / Cfg::kAccBufs) & 1;
-      if (!ptx::mbar_wait(&tmem_full[buf], uph, abort_flag, p.wait_limit_ns)) {
+      if (!ptx::mbar_wait_sleepy(&tmem_full[buf], uph, abort_flag, p.wait_limit_ns)) {
         if (lane == 0) record_error(p.err, abort_flag, kErrWaitTmemFull);
         break;
       }

@@ -95,6 +95,25 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
                : "memory");
 }
 
+// As mbar_wait, for waits expected to be long (an epilogue waiting out a
+// whole mainloop): after a short spin, back off with nanosleep between
+// probes so idle warps stop competing for issue slots and power.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity,
+                                                 volatile int* abort, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t ns = 32;
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+    __nanosleep(ns);
+    if (ns < 512) ns <<= 1;
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
