@@ -350,13 +350,22 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   const int64_t kb_total = cdiv(d->k, kBlockK);
   const int64_t batch = d->batch;
   int bn = 256, ctas = 1;
-  if (x3) {
-    bn = 128;
-  } else if (d->op != B2G_OP_GEMM) {
-    const int64_t tm = cdiv(d->m, kBlockM);
-    const int64_t t256 = tm * cdiv(d->n, 256) * batch;
-    const int64_t t128 = tm * cdiv(d->n, 128) * batch;
-    bn = (t256 * 2 < num_sms && t128 > t256) ? 128 : 256;
+  static const char* forced = std::getenv("B2G_TILE");
+  if (x3 || d->op != B2G_OP_GEMM) {
+    // Transform-warp variants (3xTF32 split, triangular masking): CTA-pair
+    // 256 x 256 units once there are at least two 128-row blocks, else one
+    // CTA with 128-wide tiles.
+    // Triangular ops stay on single-CTA 128-wide units: measured faster at
+    // N = 4096 (106 us vs 190 us for CTA pairs), whose transform warps mask
+    // twice the tile per K block.
+    const bool force_single = forced && std::strncmp(forced, "single", 6) == 0;
+    const bool force_pair = forced && std::strncmp(forced, "pair", 4) == 0;
+    if (d->m > kBlockM && !force_single && (x3 || force_pair)) {
+      ctas = 2;
+      bn = 256;
+    } else {
+      bn = 128;
+    }
   } else {
     // Cost model: waves of CTAs over the SMs times the per-SM work of one
     // unit (tile width x K blocks of its split), divided by the per-SM
@@ -372,7 +381,6 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
                           {2, 128, 0.66, 0.66}, {1, 128, 0.63, 0.63}};
     // B2G_TILE=pair512|pair256|pair128|single256|single128 pins the choice
     // (a tuning and test aid).
-    static const char* forced = std::getenv("B2G_TILE");
     double best = 0.0;
     for (const Cand& c : cands) {
       if (forced && *forced) {
@@ -399,6 +407,8 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   pl->cluster_ctas = ctas;
   if (x3)
     pl->stages = 3;
+  else if (d->op != B2G_OP_GEMM)
+    pl->stages = 6;
   else if (ctas == 2)
     pl->stages = bn == 512 ? 4 : (bn == 256 ? 6 : 8);
   else
@@ -496,6 +506,7 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.tma_store = pl.tma_store;
   p.wait_limit_ns = wait_limit_ns();
   p.inject_stall = take_injected_stall();
+  p.tri_sorted = (p.tri != kTriNone && pl.block_m == pl.block_n) ? 1 : 0;
   p.err = err_word;
 
   if (p.atomic_out) {
@@ -538,8 +549,18 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   const bool x3 = d->precision == B2G_PREC_3XTF32;
   const bool tri = p.tri != kTriNone;
   const int grid = pl.grid;
+  if (x3 && pl.cluster_ctas == 2)
+    return launch_majors<256, 3, true, true, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
   if (x3)
     return launch_majors<128, 3, true, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+#ifdef B2G_EXP_TRI_NOXF
+  if (tri && pl.cluster_ctas == 2)
+    return launch_majors<256, 6, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+  if (tri)
+    return launch_majors<128, 6, false, false, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+#endif
+  if (tri && pl.cluster_ctas == 2)
+    return launch_majors<256, 6, false, true, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
   if (pl.cluster_ctas == 2) {
     if (pl.block_n == 512)
       return launch_majors<512, 4, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
@@ -548,11 +569,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
           a_mn, b_mn, ma, mb, mc, p, grid, stream);
     return launch_majors<128, 8, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
   }
-  if (pl.block_n == 256) {
-    if (tri)
-      return launch_majors<256, 4, false, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+  if (pl.block_n == 256)
     return launch_majors<256, 4, false, false, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
-  }
   if (tri)
     return launch_majors<128, 6, false, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
   return launch_majors<128, 6, false, false, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);

@@ -62,6 +62,7 @@ struct EngineParams {
   int a_grouped, b_grouped;    // MN-major operand loaded as one 4-D box per stage
   long long wait_limit_ns;     // bound on every mbarrier wait
   int inject_stall;            // test hook: the MMA warp never signals tmem_full
+  int tri_sorted;              // triangular op on square units: longest K range first
   int* err;
 };
 
@@ -74,6 +75,38 @@ struct WorkUnit {
 // B columns in L2; split-K pieces of one tile are adjacent.  Triangular ops
 // clip the K range to the structurally non-zero band and give tiles that
 // lie wholly in the masked triangle an empty range.
+// Triangular ops on square units (block_m == block_n): enumerate the tiles
+// by decreasing K-range length so a static round-robin schedule stays
+// balanced.  Upper: tile (tm, tn) has K range [tm, tn] in units, length
+// tn - tm + 1, for d = tn - tm >= 0; lower mirrors it.  Order: d = T-1 down
+// to 0 (T - d tiles each), then the tiles wholly in the masked triangle.
+__host__ __device__ inline void decode_tri_sorted(const EngineParams& p, long long t, int* tm,
+                                                  int* tn) {
+  const int T = p.tiles_n;
+  long long rem = t;
+  int d = T - 1;
+  while (d >= 0 && rem >= T - d) {
+    rem -= T - d;
+    --d;
+  }
+  int lo, hi;            // lo: index along the diagonal, hi = lo + offset
+  if (d >= 0) {
+    lo = static_cast<int>(rem);
+    hi = lo + d;
+    if (p.tri == kTriUpper) { *tm = lo; *tn = hi; } else { *tm = hi; *tn = lo; }
+    return;
+  }
+  // Masked tiles: offsets e = 1 .. T-1 with T - e tiles each.
+  int e = 1;
+  while (e < T && rem >= T - e) {
+    rem -= T - e;
+    ++e;
+  }
+  lo = static_cast<int>(rem);
+  hi = lo + e;
+  if (p.tri == kTriUpper) { *tm = hi; *tn = lo; } else { *tm = lo; *tn = hi; }
+}
+
 __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long w) {
   WorkUnit u;
   const int split = static_cast<int>(w % p.splits);
@@ -89,6 +122,7 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
   const long long rr = r - static_cast<long long>(grp) * span;
   u.tm = first_m + static_cast<int>(rr % gsz);
   u.tn = static_cast<int>(rr / gsz);
+  if (p.tri_sorted) decode_tri_sorted(p, r, &u.tm, &u.tn);
   int lo = split * p.kb_per_split;
   int hi = lo + p.kb_per_split;
   if (hi > p.kb_total) hi = p.kb_total;
@@ -159,7 +193,7 @@ struct EngineCfg {
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(BN % 64 == 0 && BN <= (PAIR ? 512 : 256), "BN");
   static_assert(!X3 || XF, "the 3xTF32 split runs in the transform warps");
-  static_assert(!(PAIR && XF), "transform warps run in single-CTA units only");
+  static_assert(!(PAIR && XF) || kNSub == 1, "transform warps handle one B sub-tile");
 };
 
 __device__ __forceinline__ void record_error(int* err, volatile int* abort, int code) {
@@ -201,22 +235,23 @@ __device__ __forceinline__ void transform_tile(float* tile, float* lo_tile, int 
       mn_step = 1;
       k_step = 0;
     }
-    float4 v = reinterpret_cast<float4*>(tile)[c];
-    float e[4] = {v.x, v.y, v.z, v.w};
-    bool changed = false;
-    if (rule != 0) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int mn = mn_base + q * mn_step;
-        const int k = k_base + q * k_step;
-        const bool zero = (rule == 1) ? (k < mn) : (k > mn);
-        if (zero && e[q] != 0.0f) {
-          e[q] = 0.0f;
-          changed = true;
-        }
+    if (!SPLIT) {
+      // Masking only: classify the chunk's four elements first.  Wholly
+      // masked chunks are overwritten with zeros without a read; chunks with
+      // nothing masked are left alone; only chunks on the diagonal are read.
+      const int kmin = k_base, kmax = k_base + 3 * k_step;
+      const int mnmin = mn_base, mnmax = mn_base + 3 * mn_step;
+      const bool all = (rule == 1) ? (kmax < mnmin) : (kmin > mnmax);
+      const bool none = (rule == 1) ? (kmin >= mnmax) : (kmax <= mnmin);
+      if (none) continue;
+      if (all) {
+        reinterpret_cast<float4*>(tile)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        continue;
       }
     }
-    if (SPLIT) {
+    float4 v = reinterpret_cast<float4*>(tile)[c];
+    float e[4] = {v.x, v.y, v.z, v.w};
+    bool changed = false;    if (SPLIT) {
       float h[4], l[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -426,7 +461,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
-      ptx::mbar_init(&ready[s], Cfg::kXformWarps > 0 ? Cfg::kXformWarps : 1);
+      ptx::mbar_init(&ready[s], Cfg::kXformWarps > 0 ? Cfg::kXformWarps * Cfg::kCtas : 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&tmem_full[b], 1);
@@ -481,7 +516,9 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           if (!PAIR || leader) ptx::mbar_arrive(&full[s]);
           continue;
 #endif
-          if (!PAIR)
+          // Each CTA's loads complete on its own barrier when transform warps
+          // must see them; otherwise a pair's loads complete on the leader's.
+          if (!PAIR || XF)
             ptx::mbar_arrive_expect_tx(&full[s], Cfg::kStageTx);
           else if (leader)
             ptx::mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageTx);
@@ -489,14 +526,14 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           uint8_t* sb = smem + Cfg::kOffB + s * Cfg::kBBytes;
           const int k0 = kb * kBlockK;
           auto load = [&](void* dst, const CUtensorMap* map, int c0, int c1, int c2) {
-            if (PAIR)
+            if (PAIR && !XF)
               ptx::tma_load_3d_pair(dst, map, full_leader + s * 8, c0, c1, c2);
             else
               ptx::tma_load_3d(dst, map, &full[s], c0, c1, c2);
           };
           // MN-major operand as {32, K, group, batch}: one box of all groups.
           auto load_grouped = [&](void* dst, const CUtensorMap* map, int g0, int c3) {
-            if (PAIR)
+            if (PAIR && !XF)
               ptx::tma_load_4d_pair(dst, map, full_leader + s * 8, 0, k0, g0, c3);
             else
               ptx::tma_load_4d(dst, map, &full[s], 0, k0, g0, c3);
@@ -530,7 +567,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       // exit, also when another role gave up early (bounded; a no-op on the
       // normal path, where the MMA warp already waited for each of them).
       // The pair leader's barriers also count the peer's loads.
-      if (!PAIR || leader) {
+      if (!PAIR || XF || leader) {
         volatile int never = 0;
         const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
         for (uint32_t j = first; j < it; ++j)
@@ -603,8 +640,13 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
             if (X3) {
               const uint64_t dal = ptx::smem_desc(sal + k8 * a_kstep, a_lbo, a_sbo, a_lay);
               const uint64_t dbl = ptx::smem_desc(sbl + k8 * b_kstep, b_lbo, b_sbo, b_lay);
-              ptx::mma_tf32(d_tmem, da, dbl, idesc, 1);
-              ptx::mma_tf32(d_tmem, dal, db, idesc, 1);
+              if (PAIR) {
+                ptx::mma_tf32_pair(d_tmem, da, dbl, idesc, 1);
+                ptx::mma_tf32_pair(d_tmem, dal, db, idesc, 1);
+              } else {
+                ptx::mma_tf32(d_tmem, da, dbl, idesc, 1);
+                ptx::mma_tf32(d_tmem, dal, db, idesc, 1);
+              }
             }
           }
           if (PAIR)
@@ -731,13 +773,16 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
     if (lane == 0) ptx::bulk_wait_read<0>();   // staging boxes read before the CTA exits
   } else if (XF) {
     // ------------------------------------------------------------ transform
+    // Each CTA transforms its own slices (A rows m_cta.., B columns n_cta..)
+    // and then signals the MMA issuer's ready[s] (the leader's in a pair).
     const int xt = threadIdx.x - (2 + Cfg::kEpiWarps) * 32;
+    const uint32_t ready_leader = PAIR ? ptx::mapa_shared(ptx::smem_addr(ready), 0) : 0u;
     uint32_t it = 0;
     bool ok = true;
     for (long long w = unit0; w < p.work_units && ok; w += unit_step) {
       const WorkUnit u = decode_unit(p, w);
-      const int m0 = u.tm * Cfg::kUnitM;
-      const int n0 = u.tn * BN;
+      const int m0 = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM;
+      const int n0 = u.tn * BN + static_cast<int>(rank) * Cfg::kSubCols;
       for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -753,17 +798,25 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           if (k0 + kBlockK - 1 > n0) rule_b = 2;
         } else if (p.tri == kTriLower) {   // A: zero k > i ; B: zero k < j
           if (k0 + kBlockK - 1 > m0) rule_a = 2;
-          if (k0 < n0 + BN - 1) rule_b = 1;
+          if (k0 < n0 + Cfg::kBnCta - 1) rule_b = 1;
         }
         float* ta = reinterpret_cast<float*>(smem + Cfg::kOffA + s * Cfg::kABytes);
         float* tb = reinterpret_cast<float*>(smem + Cfg::kOffB + s * Cfg::kBBytes);
         float* tal = reinterpret_cast<float*>(smem + Cfg::kOffALo + s * Cfg::kABytes);
         float* tbl = reinterpret_cast<float*>(smem + Cfg::kOffBLo + s * Cfg::kBBytes);
         transform_tile<A_MN, kBlockM, X3>(ta, tal, m0, k0, rule_a, xt);
-        transform_tile<B_MN, BN, X3>(tb, tbl, n0, k0, rule_b, xt);
-        ptx::fence_proxy_async_smem();
+        transform_tile<B_MN, Cfg::kBnCta, X3>(tb, tbl, n0, k0, rule_b, xt);
+        if (PAIR)
+          asm volatile("fence.proxy.async;" ::: "memory");   // visible to the pair's MMA
+        else
+          ptx::fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&ready[s]);
+        if (lane == 0) {
+          if (PAIR)
+            ptx::mbar_arrive_cluster(ready_leader + s * 8);
+          else
+            ptx::mbar_arrive(&ready[s]);
+        }
       }
     }
   }

@@ -115,7 +115,7 @@ def test_plan_misaligned_base_pointer_is_staged(capi):
 
 def test_plan_3xtf32_uses_narrow_tiles(capi):
     p = _plan(capi, 2048, 2048, 2048, precision=capi.PREC_3XTF32)
-    assert p.block_n == 128 and p.stages == 3 and p.cluster_ctas == 1
+    assert p.block_n == 256 and p.stages == 3 and p.cluster_ctas == 2
 
 
 def test_plan_batched(capi):
