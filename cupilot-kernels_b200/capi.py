@@ -68,6 +68,11 @@ def lib(path: Path | None = None) -> C.CDLL:
         h.b2g_rowscale.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                    C.c_int64, C.c_int64, C.c_void_p]
         h.b2g_rowscale.restype = C.c_int
+        h.b2g_gemv.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int64,
+                               C.c_int64, C.c_void_p]
+        h.b2g_gemv.restype = C.c_int
+        h.b2g_scale.argtypes = [C.c_void_p, C.c_float, C.c_void_p, C.c_int64, C.c_void_p]
+        h.b2g_scale.restype = C.c_int
         h.b2g_read_device_error.argtypes = [C.c_int, C.POINTER(C.c_int32)]
         h.b2g_read_device_error.restype = C.c_int
         h.b2g_status_string.argtypes = [C.c_int]

@@ -251,7 +251,20 @@ __device__ __forceinline__ void transform_tile(float* tile, float* lo_tile, int 
     }
     float4 v = reinterpret_cast<float4*>(tile)[c];
     float e[4] = {v.x, v.y, v.z, v.w};
-    bool changed = false;    if (SPLIT) {
+    bool changed = false;
+    if (rule != 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int mn = mn_base + q * mn_step;
+        const int k = k_base + q * k_step;
+        const bool zero = (rule == 1) ? (k < mn) : (k > mn);
+        if (zero && e[q] != 0.0f) {
+          e[q] = 0.0f;
+          changed = true;
+        }
+      }
+    }
+    if (SPLIT) {
       float h[4], l[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {

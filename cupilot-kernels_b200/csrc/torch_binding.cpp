@@ -251,6 +251,40 @@ at::Tensor diag_matmul(at::Tensor A, at::Tensor B) {
   return out;
 }
 
+// kernels/4_Matrix_vector_multiplication_best_kernel.cu:84 — C (M, 1) = A (M, K) . B (K, 1)
+at::Tensor gemv(at::Tensor A, at::Tensor B) {
+  check_input(A, "A");
+  check_input(B, "B");
+  TORCH_CHECK(A.dim() == 2, "A must be 2D");
+  TORCH_CHECK(B.dim() == 2, "B must be 2D");
+  TORCH_CHECK(B.size(0) == A.size(1), "A and B shapes not matched");
+  TORCH_CHECK(B.size(1) == 1, "B must be a column vector");
+  TORCH_CHECK(A.device() == B.device(), "A and B must be on the same device");
+  const c10::cuda::CUDAGuard guard(A.device());
+  at::Tensor a = A.stride(1) == 1 ? A : A.contiguous();
+  at::Tensor x = B.contiguous();
+  at::Tensor C = at::empty({A.size(0), 1}, A.options());
+  auto stream = at::cuda::getCurrentCUDAStream(A.device().index());
+  check_status(b2g_gemv(a.data_ptr<float>(), std::max<int64_t>(a.stride(0), A.size(1)),
+                        x.data_ptr<float>(), C.data_ptr<float>(), A.size(0), A.size(1),
+                        stream.stream()),
+               "b2g_gemv");
+  return C;
+}
+
+// kernels/5_Matrix_scalar_multiplication_best_kernel.cu:47 — C = A * s
+at::Tensor matrix_scalar_mult(at::Tensor A, double s) {
+  check_input(A, "A");
+  TORCH_CHECK(A.is_contiguous(), "A must be contiguous");
+  const c10::cuda::CUDAGuard guard(A.device());
+  at::Tensor C = at::empty_like(A);
+  auto stream = at::cuda::getCurrentCUDAStream(A.device().index());
+  check_status(b2g_scale(A.data_ptr<float>(), static_cast<float>(s), C.data_ptr<float>(),
+                         A.numel(), stream.stream()),
+               "b2g_scale");
+  return C;
+}
+
 // Generic entry: op(A) . op(B) with explicit flags (used by the partitioner).
 at::Tensor gemm(at::Tensor A, at::Tensor B, bool trans_a, bool trans_b, int64_t op) {
   return matmul_2d(trans_a ? A.t() : A, trans_b ? B.t() : B, static_cast<int>(op));
@@ -289,6 +323,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("matmul_transposed_a", &matmul_transposed_a);
   m.def("matmul_transposed_b", &matmul_transposed_b);
   m.def("matmul_transposed_both", &matmul_transposed_both);
+  m.def("gemv", &gemv);
+  m.def("matrix_scalar_mult", &matrix_scalar_mult);
   m.def("gemm", &gemm, "op(A) . op(B)", py::arg("A"), py::arg("B"), py::arg("trans_a") = false,
         py::arg("trans_b") = false, py::arg("op") = 0);
   m.def("set_precision", &set_precision);

@@ -75,6 +75,10 @@ class Operator:
 
 _K = "kernels/"
 OPERATORS = {
+    4: Operator(4, "gemv", "gemv_cuda",
+                _K + "4_Matrix_vector_multiplication_best_kernel.cu:84", _ext.gemv),
+    5: Operator(5, "matrix_scalar", "matrix_scalar_mult_cuda",
+                _K + "5_Matrix_scalar_multiplication_best_kernel.cu:47", _ext.matrix_scalar_mult),
     1: Operator(1, "square", "matmul_cuda",
                 _K + "1_Square_matrix_multiplication_best_kernel.cu:189", _ext.square_matmul),
     2: Operator(2, "standard", "matmul_cuda",

@@ -28,6 +28,8 @@
  *   kernels/16_Matmul_with_transposed_A_best_kernel.cu:124      matmul_transposed_cuda   -> b2g_gemm (TN)
  *   kernels/17_Matmul_with_transposed_B_best_kernel.cu:267      matmul_cuda              -> b2g_gemm (NT)
  *   kernels/18_Matmul_with_transposed_both_best_kernel.cu:152   matmul_transposed_cuda   -> b2g_gemm (TT)
+ *   kernels/4_Matrix_vector_multiplication_best_kernel.cu:84    gemv_cuda                -> b2g_gemv
+ *   kernels/5_Matrix_scalar_multiplication_best_kernel.cu:47    matrix_scalar_mult_cuda  -> b2g_scale
  *
  * Error behaviour: every entry point returns a b2g_status; 0 is success.
  * Nothing traps or asserts on the device.  Kernel-side waits are bounded;
@@ -156,6 +158,19 @@ B2G_API int b2g_rowscale(const float* d, const float* b, float* out, int64_t row
  */
 #define B2G_NOALLOC_SCRATCH_BYTES (16ll << 20)
 B2G_API int b2g_gemm_noalloc(const b2g_gemm_desc* desc, b2g_stream_t stream);
+
+/*
+ * y[i] = sum_k A[i][k] x[k]  (fp32 CUDA-core dot products, 16-byte streaming loads).
+ * Replaces gemv_cuda (kernels/4_Matrix_vector_multiplication_best_kernel.cu:84).
+ */
+B2G_API int b2g_gemv(const float* a, int64_t lda, const float* x, float* y, int64_t m,
+                     int64_t k, b2g_stream_t stream);
+
+/*
+ * out[i] = a[i] * s for n contiguous elements, one rounding per element.
+ * Replaces matrix_scalar_mult_cuda (kernels/5_Matrix_scalar_multiplication_best_kernel.cu:47).
+ */
+B2G_API int b2g_scale(const float* a, float s, float* out, int64_t n, b2g_stream_t stream);
 
 /* Read and clear the device-side error word of `device` (synchronises it). */
 B2G_API int b2g_read_device_error(int device, int32_t* code);

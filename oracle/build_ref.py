@@ -30,6 +30,8 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
 # PID -> (file, Part-3 function name, file:line of that function)
 REF_FUNCS = {
+    4: ("4_Matrix_vector_multiplication_best_kernel.cu", "gemv_cuda", 84),
+    5: ("5_Matrix_scalar_multiplication_best_kernel.cu", "matrix_scalar_mult_cuda", 47),
     1: ("1_Square_matrix_multiplication_best_kernel.cu", "matmul_cuda", 189),
     2: ("2_Standard_matrix_multiplication_best_kernel.cu", "matmul_cuda", 117),
     3: ("3_Batched_matrix_multiplication_best_kernel.cu", "batched_matmul_cuda", 113),
@@ -80,9 +82,10 @@ def build_one(pid: int, verbose: bool = False, force: bool = False) -> Path:
     name = target.name.split(".")[0]
     obj = OUT / f"ref_p{pid}.o"
     shim = OUT / f"ref_p{pid}_shim.cpp"
+    second = "float s" if pid == 5 else "torch::Tensor B"   # K5 takes a scalar (K5:47)
     shim.write_text(
         "#include <torch/extension.h>\n"
-        f"torch::Tensor {func}(torch::Tensor A, torch::Tensor B);\n"
+        f"torch::Tensor {func}(torch::Tensor A, {second});\n"
         f"PYBIND11_MODULE({name}, m) {{ m.def(\"{func}\", &{func}); }}\n")
     inc = [f"-I{i}" for i in incs]
     nvcc = [str(CUDA_HOME / "bin" / "nvcc"), "-gencode", "arch=compute_100a,code=sm_100a",

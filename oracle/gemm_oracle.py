@@ -38,6 +38,16 @@ def _f64(x):
     return np.asarray(x, dtype=np.float64)
 
 
+def gemv(A, B):
+    """C (M, 1) = A (M, K) . B (K, 1)          kernels/4_...:84"""
+    return _f64(A) @ _f64(B)
+
+
+def matrix_scalar(A, s):
+    """C = A * s in fp32, one rounding per element   kernels/5_...:47"""
+    return (np.asarray(A, dtype=np.float32) * np.float32(s)).astype(np.float32)
+
+
 def matmul(A, B):
     return _f64(A) @ _f64(B)
 
@@ -91,6 +101,7 @@ def transposed_both(A, B):
 
 
 BY_PID = {
+    4: gemv, 5: matrix_scalar,
     1: square, 2: standard, 3: batched, 6: large_k, 7: small_k, 8: irregular,
     9: tall_skinny, 10: tensor3d, 11: tensor4d, 12: diag, 13: symmetric,
     14: upper_tri, 15: lower_tri, 16: transposed_a, 17: transposed_b, 18: transposed_both,

@@ -63,6 +63,13 @@ cases.append({"pid": 10, "name": "tensor3d", "A": [[[1.0, 2.0]], [[3.0, 4.0]]],
               "B": [[1.0, 0.0, 1.0], [0.0, 1.0, 1.0]],
               "C": [[[1.0, 2.0, 3.0]], [[3.0, 4.0, 7.0]]]})
 
+# GEMV: [[1,2,3],[4,5,6]] . [1,0,-1]^T = [-2, -2]
+cases.append({"pid": 4, "name": "gemv", "A": [[1.0, 2.0, 3.0], [4.0, 5.0, 6.0]],
+              "B": [[1.0], [0.0], [-1.0]], "C": [[-2.0], [-2.0]]})
+# Matrix x scalar.
+cases.append({"pid": 5, "name": "scalar", "A": [[1.0, -2.0], [0.5, 3.0]], "B": 4.0,
+              "C": [[4.0, -8.0], [2.0, 12.0]]})
+
 out = Path(__file__).with_name("known_answers.json")
 out.write_text(json.dumps({"cases": cases}, indent=0))
 print(f"wrote {len(cases)} cases to {out}")

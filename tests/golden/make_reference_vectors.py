@@ -8,7 +8,11 @@ stores its output (row subsets for the larger ones).  Shapes stay inside
 each reference kernel's own contract (tile multiples, K7's K = 64, K9's
 inner dimension <= 32, K16's block swizzle needing M and N multiples of 512,
 kernels/16_Matmul_with_transposed_A_best_kernel.cu:18-40).  K2 is skipped: its shape is hard-coded
-(kernels/2_Standard_matrix_multiplication_best_kernel.cu:16-18).
+(kernels/2_Standard_matrix_multiplication_best_kernel.cu:16-18).  K4 is
+not run: its first call here (M = 96, K = 1024) raised an illegal memory
+access on a B200 although reading its kernel shows no out-of-range index at
+that shape, so it stays off the GPU; PID 4 is pinned by its closed-form
+known answer.
 
     python tests/golden/make_reference_vectors.py
 """
@@ -23,7 +27,9 @@ sys.path.insert(0, str(REPO))
 
 # pid -> (list of input shapes, rows of the output to keep); at most 64 rows
 # are stored to keep the fixture small.
+SCALE = 2.5   # the scalar operand of K5
 CASES = {
+    5: ([(64, 256)], 64),
     1: ([(256, 256), (256, 256)], 64),
     3: ([(2, 256, 64), (2, 64, 256)], 64),
     6: ([(64, 2048), (2048, 64)], 64),
@@ -47,6 +53,8 @@ def inputs(pid):
     g = torch.Generator().manual_seed(SEED0 + pid)
     shapes, _ = CASES[pid]
     ts = [torch.randn(*s, generator=g) for s in shapes]
+    if pid == 5:
+        ts.append(SCALE)
     if pid == 13:
         ts = [(t + t.T) / 2 for t in ts]
     if pid == 14:
@@ -63,7 +71,7 @@ def main():
     for pid, (_, keep) in CASES.items():
         f = build_ref.load(pid)
         A, B = inputs(pid)
-        C = f(A.cuda(), B.cuda())
+        C = f(A.cuda(), B if pid == 5 else B.cuda())
         torch.cuda.synchronize()
         C = C.cpu().numpy()
         if keep is not None:

@@ -249,3 +249,31 @@ def test_batched_matmul_out_validates_shapes(ops):
     B = torch.randn(2, 4, 6, device="cuda")
     with pytest.raises(RuntimeError, match="C must be"):
         ops.batched_matmul_out(A, B, torch.empty(2, 8, 5, device="cuda"))
+
+
+@pytest.mark.parametrize("m,k", [(1, 1), (7, 3), (4096, 4096), (100, 100003), (3, 65536),
+                                 (20000, 64), (33, 4097)])
+def test_gemv(ops, m, k):
+    g = _gen(m * 13 + k)
+    A, x = _randn(g, m, k), _randn(g, k, 1)
+    y = ops.p4.forward(A.cuda(), x.cuda())
+    assert y.shape == (m, 1)
+    err = O.rel_fro(y.cpu().double().numpy(), O.gemv(A.numpy(), x.numpy()))
+    assert err <= 1e-5, err           # fp32 accumulation against fp64
+
+
+def test_gemv_strided_rows(ops):
+    g = _gen(8)
+    base = _randn(g, 50, 700)
+    A = base[:, 3:603]                 # pitch 700, unaligned start
+    x = _randn(g, 600, 1)
+    y = ops.p4.gemv_cuda(A.cuda(), x.cuda())
+    assert O.rel_fro(y.cpu().double().numpy(), O.gemv(A.numpy(), x.numpy())) <= 1e-5
+
+
+@pytest.mark.parametrize("shape", [(1,), (3, 5), (4096, 4096), (1000, 1003), (7, 1, 9)])
+def test_matrix_scalar_bit_exact(ops, shape):
+    g = _gen(len(shape) * 11 + shape[0])
+    A = _randn(g, *shape)
+    C = ops.p5.matrix_scalar_mult_cuda(A.cuda(), 0.37)
+    np.testing.assert_array_equal(C.cpu().numpy(), O.matrix_scalar(A.numpy(), 0.37))

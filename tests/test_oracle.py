@@ -17,7 +17,8 @@ def _cases():
 @pytest.mark.parametrize("case", _cases(), ids=lambda c: f"p{c['pid']}-{c['name']}")
 def test_known_answers(case):
     f = O.BY_PID[case["pid"]]
-    got = f(np.array(case["A"], dtype=np.float32), np.array(case["B"], dtype=np.float32))
+    B = case["B"] if case["pid"] == 5 else np.array(case["B"], dtype=np.float32)
+    got = f(np.array(case["A"], dtype=np.float32), B)
     np.testing.assert_array_equal(np.asarray(got, dtype=np.float64), np.array(case["C"]))
 
 

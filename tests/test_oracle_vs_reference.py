@@ -28,12 +28,12 @@ REF = np.load(GOLD / "reference_outputs.npz")
 
 @pytest.mark.parametrize("pid", sorted(gen.CASES))
 def test_oracle_agrees_with_reference_kernel(pid):
-    A, B = (t.numpy() for t in gen.inputs(pid))
+    A, B = (t.numpy() if hasattr(t, "numpy") else t for t in gen.inputs(pid))
     ref = REF[f"p{pid}"]
     want = np.asarray(O.BY_PID[pid](A, B))
     want = want[..., : ref.shape[-2], :]
     assert want.shape == ref.shape
-    if pid == 12:
+    if pid in (5, 12):           # one fp32 rounding per element: bit-exact
         np.testing.assert_array_equal(ref, want.astype(np.float32))
         return
     err = O.rel_fro(ref, want)
