@@ -211,6 +211,10 @@ def device_inputs(w, seed_offset=0, **shapes):
         return r(s["b"], s["i"], s["j"], s["l"]), r(s["l"], s["k"])
     if n == "diag":
         return r(s["n"]), r(s["n"], s["n"])
+    if n == "gemv":
+        return r(s["m"], s["k"]), r(s["k"], 1)
+    if n == "matrix_scalar":
+        return r(s["m"], s["n"]), 2.5
     if n == "upper_tri":
         return torch.triu(r(s["n"], s["n"])), torch.triu(r(s["n"], s["n"]))
     if n == "lower_tri":
@@ -231,6 +235,8 @@ def cublas_fn(name, A, B):
         return lambda: torch.matmul(A.t(), B.t())
     if name == "diag":
         return lambda: A[:, None] * B
+    if name == "matrix_scalar":
+        return lambda: A * B
     if name == "upper_tri":
         return lambda: torch.triu(torch.matmul(A, B))
     if name == "lower_tri":
@@ -256,7 +262,8 @@ def roofline(w, ms, peaks, flops=None, nbytes=None):
 
 
 # ---------------------------------------------------------------- reference kernels
-REF_SAFE = {  # workload -> (pid, how to adapt inputs to the reference kernel's contract)
+REF_SAFE = {  # workload -> reference PID whose kernel runs on the workload
+    "matrix_scalar": 5,
     "square": 1, "batched": 3, "large_k": 6, "small_k": 7, "irregular": 8, "tall_skinny": 9,
     "tensor3d": 10, "tensor4d": 11, "diag": 12, "symmetric": 13, "upper_tri": 14,
     "lower_tri": 15, "transposed_a": 16, "transposed_b": 17, "transposed_both": 18,
@@ -266,6 +273,10 @@ REF_SAFE = {  # workload -> (pid, how to adapt inputs to the reference kernel's 
 def reference_callable(name, A, B):
     from oracle import build_ref
 
+    if name == "gemv":
+        # K4 raised an illegal memory access on its first golden-vector call
+        # on this GPU type (kernels/4_...:84); it is not run again.
+        raise RuntimeError("reference K4 (gemv_cuda) faulted on a B200 and is not run")
     pid = REF_SAFE[name]
     f = build_ref.load(pid)
     if name == "small_k":

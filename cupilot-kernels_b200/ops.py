@@ -145,6 +145,29 @@ def _host_streams(device):
     return _HOST_STREAMS[key]
 
 
+_HOST_BUFFERS = {}
+
+
+def _host_buffers(dev, sa, sb, sc):
+    """Device staging for batched_matmul_from_host, kept per device and grown
+    on demand: back-to-back calls reuse it instead of allocating ~2 GB each
+    time (the upload stream is ordered after the previous call's downloads)."""
+    import math
+
+    import torch
+
+    na, nb, nc = math.prod(sa), math.prod(sb), math.prod(sc)
+    # 256-byte aligned sub-buffers (64 floats)
+    pa, pb = (na + 63) // 64 * 64, (nb + 63) // 64 * 64
+    need = pa + pb + nc
+    buf = _HOST_BUFFERS.get(dev.index)
+    if buf is None or buf.numel() < need:
+        _HOST_BUFFERS[dev.index] = None
+        buf = torch.empty(need, dtype=torch.float32, device=dev)
+        _HOST_BUFFERS[dev.index] = buf
+    return (buf[:na].view(sa), buf[pa:pa + nb].view(sb), buf[pa + pb:pa + pb + nc].view(sc))
+
+
 def torch_device_index(device):
     import torch
 
@@ -180,14 +203,13 @@ def batched_matmul_from_host(A_h, B_h, out=None, chunks=8, device=None, synchron
     if bs == 0:
         return out
     s_in, s_mm, s_out = _host_streams(dev)
-    A_d = torch.empty(bs, M, K, dtype=torch.float32, device=dev)
-    B_d = torch.empty(bs, K, N, dtype=torch.float32, device=dev)
-    C_d = torch.empty(bs, M, N, dtype=torch.float32, device=dev)
+    A_d, B_d, C_d = _host_buffers(dev, (bs, M, K), (bs, K, N), (bs, M, N))
     step = max(1, (bs + chunks - 1) // chunks)
     pieces = [(b0, min(bs, b0 + step)) for b0 in range(0, bs, step)]
     cur = torch.cuda.current_stream(dev)
     for s in (s_in, s_mm, s_out):
         s.wait_stream(cur)
+    s_in.wait_stream(s_out)   # the previous call's downloads are done with the buffers
     for b0, b1 in pieces:
         with torch.cuda.stream(s_in):
             A_d[b0:b1].copy_(A_h[b0:b1], non_blocking=True)
@@ -198,11 +220,6 @@ def batched_matmul_from_host(A_h, B_h, out=None, chunks=8, device=None, synchron
         s_out.wait_stream(s_mm)
         with torch.cuda.stream(s_out):
             out[b0:b1].copy_(C_d[b0:b1], non_blocking=True)
-    for t in (A_d, B_d):
-        t.record_stream(s_in)
-        t.record_stream(s_mm)
-    C_d.record_stream(s_mm)
-    C_d.record_stream(s_out)
     cur.wait_stream(s_out)
     if synchronize:
         s_out.synchronize()

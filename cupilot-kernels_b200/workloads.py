@@ -91,6 +91,14 @@ def _mk_sym(g, n):
     return (X + X.T) / 2, (Y + Y.T) / 2
 
 
+def _mk_gemv(g, m, k):
+    return _randn(g, m, k), _randn(g, k, 1)
+
+
+def _mk_scalar(g, m, n):
+    return _randn(g, m, n), 2.5
+
+
 def _gemm_cost(m, n, k, batch=1, a_shared=False, b_shared=False):
     flops = 2.0 * m * n * k * batch
     a = m * k * (1 if a_shared else batch)
@@ -143,6 +151,14 @@ _add(_w("tensor4d", 11, dict(b=16, i=256, j=512, l=256, k=768), 14, _mk_4d,
         _gemm_cost(16 * 256 * 512, 768, 256), "hbm"))
 
 
+# Next rows (reference PIDs 4-5; no benchmark config names their sizes, so
+# these are chosen HBM-bound sizes: a 1 GiB fp32 matrix streamed once).
+_add(Workload("gemv", 4, dict(m=16384, k=16384), 15, _mk_gemv, 2.0 * 16384 * 16384,
+              4.0 * (16384 * 16384 + 16384 + 16384), "hbm"))
+_add(Workload("matrix_scalar", 5, dict(m=16384, n=16384), 16, _mk_scalar, 16384.0 * 16384,
+              4.0 * 2 * 16384 * 16384, "hbm"))
+
+
 def cost_for(name: str, **shapes) -> Tuple[float, float]:
     """(flops, min_bytes) of a workload at overridden shapes."""
     w = WORKLOADS[name]
@@ -160,5 +176,9 @@ def cost_for(name: str, **shapes) -> Tuple[float, float]:
     if name == "diag":
         n = s["n"]
         return float(n * n), 4.0 * (n + 2 * n * n)
+    if name == "gemv":
+        return 2.0 * s["m"] * s["k"], 4.0 * (s["m"] * s["k"] + s["m"] + s["k"])
+    if name == "matrix_scalar":
+        return float(s["m"] * s["n"]), 8.0 * s["m"] * s["n"]
     n = s["n"]
     return _gemm_cost(n, n, n)
