@@ -16,6 +16,8 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <queue>
+#include <vector>
 
 #include "../../include/b2g_gemm.h"
 #include "gemm_engine.cuh"
@@ -31,6 +33,7 @@ namespace b2g {
 namespace {
 
 constexpr int kMaxDevices = 64;
+constexpr int kTriDiagBlock = 128;   // diagonal-block width of the triangular masking copies
 
 inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
@@ -171,6 +174,50 @@ __global__ void pitch_copy_kernel(const float* __restrict__ src, float* __restri
   }
 }
 
+// ---------------------------------------------------------------- triangular diagonal blocks
+// Masked copies of the 128 x 128 diagonal blocks of A and B (a row-major
+// n x 128 array each: row r of block b holds src[b*128 + r][b*128 + c]).
+// Upper: keep column >= row in both (A: k >= i, B: k <= j); lower: keep
+// column <= row.  Columns past n are zero.  blockIdx.y selects A or B.
+// Triangular pre-pass, one launch.  blockIdx.y 0 / 1: kTriDiagRows rows of
+// one diagonal block of A / B into its masked copy.  blockIdx.y 2: one
+// kTriDiagRows-row slice of a split tile's C region set to zero (the tile's
+// K pieces then reduce-add into it).  Blocks past their y's work exit.
+constexpr int kTriDiagRows = 8;
+__global__ void __launch_bounds__(256) tri_prepare_kernel(
+    const float* __restrict__ a, int64_t lda, const float* __restrict__ b, int64_t ldb, int64_t n,
+    int upper, float* __restrict__ adiag, float* __restrict__ bdiag, float* __restrict__ c,
+    int64_t ldc, const int2* __restrict__ split_tiles, int n_split, int block_m, int block_n) {
+  constexpr int kSlices = kTriDiagBlock / kTriDiagRows;
+  if (blockIdx.y == 2) {
+    const int slices = (block_m + kTriDiagRows - 1) / kTriDiagRows;
+    if (static_cast<int>(blockIdx.x) >= n_split * slices) return;
+    const int2 t = split_tiles[blockIdx.x / slices];
+    const int r0 = (blockIdx.x % slices) * kTriDiagRows;
+    for (int idx = threadIdx.x; idx < kTriDiagRows * block_n; idx += blockDim.x) {
+      const int r = r0 + idx / block_n;
+      const int64_t row = static_cast<int64_t>(t.x) * block_m + r;
+      const int64_t col = static_cast<int64_t>(t.y) * block_n + idx % block_n;
+      if (r < block_m && row < n && col < n) c[row * ldc + col] = 0.f;
+    }
+    return;
+  }
+  if (static_cast<int64_t>(blockIdx.x) >= ((n + kTriDiagBlock - 1) / kTriDiagBlock) * kSlices)
+    return;
+  const float* src = blockIdx.y == 0 ? a : b;
+  const int64_t ld = blockIdx.y == 0 ? lda : ldb;
+  float* dst = blockIdx.y == 0 ? adiag : bdiag;
+  const int64_t base = static_cast<int64_t>(blockIdx.x / kSlices) * kTriDiagBlock;
+  const int r0 = (blockIdx.x % kSlices) * kTriDiagRows;
+  for (int idx = threadIdx.x; idx < kTriDiagRows * kTriDiagBlock; idx += blockDim.x) {
+    const int r = r0 + idx / kTriDiagBlock, cc = idx % kTriDiagBlock;
+    const int64_t gi = base + r, gc = base + cc;
+    if (gi >= n) break;
+    const bool keep = upper ? (cc >= r) : (cc <= r);
+    dst[gi * kTriDiagBlock + cc] = (keep && gc < n) ? __ldg(src + gi * ld + gc) : 0.0f;
+  }
+}
+
 // ---------------------------------------------------------------- row scale
 // out[i][j] = d[i] * B[i][j]; 16-byte loads/stores when the layout allows.
 __global__ void __launch_bounds__(256) rowscale_vec_kernel(const float* __restrict__ d,
@@ -218,7 +265,8 @@ __global__ void rowscale_scalar_kernel(const float* __restrict__ d, const float*
 // ---------------------------------------------------------------- engine instantiations
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG>
 int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
-                  const EngineParams& p, int grid, cudaStream_t stream) {
+                  const CUtensorMap& mad, const CUtensorMap& mbd, const EngineParams& p, int grid,
+                  cudaStream_t stream) {
   using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>;
   auto kern = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>;
   static thread_local int configured_dev = -1;
@@ -244,20 +292,99 @@ int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p) != cudaSuccess) return B2G_ERR_LAUNCH;
+  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mad, mbd, p) != cudaSuccess)
+    return B2G_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
 }
 
 template <int BN, int STAGES, bool X3, bool XF, bool PAIR, int EPIG = 1>
-int launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb,
-                  const CUtensorMap& mc, const EngineParams& p, int grid, cudaStream_t st) {
+int launch_majors(bool a_mn, bool b_mn, const CUtensorMap (&m)[5], const EngineParams& p,
+                  int grid, cudaStream_t st) {
   if (!a_mn && !b_mn)
-    return launch_engine<BN, STAGES, false, false, X3, XF, PAIR, EPIG>(ma, mb, mc, p, grid, st);
+    return launch_engine<BN, STAGES, false, false, X3, XF, PAIR, EPIG>(m[0], m[1], m[2], m[3],
+                                                                        m[4], p, grid, st);
   if (!a_mn && b_mn)
-    return launch_engine<BN, STAGES, false, true, X3, XF, PAIR, EPIG>(ma, mb, mc, p, grid, st);
+    return launch_engine<BN, STAGES, false, true, X3, XF, PAIR, EPIG>(m[0], m[1], m[2], m[3],
+                                                                       m[4], p, grid, st);
   if (a_mn && !b_mn)
-    return launch_engine<BN, STAGES, true, false, X3, XF, PAIR, EPIG>(ma, mb, mc, p, grid, st);
-  return launch_engine<BN, STAGES, true, true, X3, XF, PAIR, EPIG>(ma, mb, mc, p, grid, st);
+    return launch_engine<BN, STAGES, true, false, X3, XF, PAIR, EPIG>(m[0], m[1], m[2], m[3],
+                                                                       m[4], p, grid, st);
+  return launch_engine<BN, STAGES, true, true, X3, XF, PAIR, EPIG>(m[0], m[1], m[2], m[3], m[4],
+                                                                    p, grid, st);
+}
+
+// Unit table for triangular ops: every tile's K range (the engine's own
+// clipping), tiles longer than the mean load per cluster cut into K pieces
+// (which then reduce-add into a pre-zeroed C region), and a longest-first
+// greedy assignment to the least-loaded cluster.  Entry r * clusters + c is
+// cluster c's r-th unit (padding entries are skips), matching the kernel's
+// static stride over units.
+struct TriTable {
+  std::vector<int4> units;
+  std::vector<int2> split_tiles;
+};
+
+TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int tiles_m,
+                         int tiles_n, int clusters, bool allow_split) {
+  EngineParams q;
+  std::memset(&q, 0, sizeof(q));
+  q.K = static_cast<int>(d->k);
+  q.block_m = block_m;
+  q.block_n = block_n;
+  q.tiles_m = tiles_m;
+  q.tiles_n = tiles_n;
+  q.splits = 1;
+  q.kb_total = static_cast<int>(cdiv(d->k, kBlockK));
+  q.kb_per_split = std::max(q.kb_total, 1);
+  q.group_m = 8;
+  q.tri = d->op == B2G_OP_TRI_UPPER ? kTriUpper : kTriLower;
+  struct Item { int tm, tn, lo, hi, flags, weight; };
+  std::vector<Item> items;
+  const int64_t ntiles = static_cast<int64_t>(tiles_m) * tiles_n;
+  int64_t total = 0;
+  std::vector<WorkUnit> tiles(ntiles);
+  for (int64_t t = 0; t < ntiles; ++t) {
+    tiles[t] = decode_unit(q, t);
+    total += tiles[t].kb_hi - tiles[t].kb_lo;
+  }
+  const int64_t lmax = allow_split ? std::max<int64_t>(8, cdiv(total, clusters)) : (1ll << 40);
+  TriTable out;
+  for (const WorkUnit& u : tiles) {
+    const int len = u.kb_hi - u.kb_lo;
+    if (len == 0) {
+      items.push_back({u.tm, u.tn, 0, 0, 0, 2});   // zero tile: epilogue work only
+      continue;
+    }
+    const int np = static_cast<int>(cdiv(len, lmax));
+    if (np > 1) out.split_tiles.push_back(make_int2(u.tm, u.tn));
+    for (int j = 0; j < np; ++j) {
+      const int lo = u.kb_lo + static_cast<int>(static_cast<int64_t>(len) * j / np);
+      const int hi = u.kb_lo + static_cast<int>(static_cast<int64_t>(len) * (j + 1) / np);
+      items.push_back({u.tm, u.tn, lo, hi, np > 1 ? kUnitAccumulate : 0, hi - lo + 2});
+    }
+  }
+  std::stable_sort(items.begin(), items.end(),
+                   [](const Item& x, const Item& y) { return x.weight > y.weight; });
+  using Load = std::pair<int64_t, int>;   // (load, cluster)
+  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+  for (int c = 0; c < clusters; ++c) heap.push({0, c});
+  std::vector<std::vector<int>> per(clusters);
+  for (int i = 0; i < static_cast<int>(items.size()); ++i) {
+    Load l = heap.top();
+    heap.pop();
+    per[l.second].push_back(i);
+    l.first += items[i].weight;
+    heap.push(l);
+  }
+  size_t rounds = 0;
+  for (const auto& v : per) rounds = std::max(rounds, v.size());
+  out.units.assign(rounds * clusters, make_int4(0, 0, 0, kUnitSkip << 24));
+  for (int c = 0; c < clusters; ++c)
+    for (size_t r = 0; r < per[c].size(); ++r) {
+      const Item& it = items[per[c][r]];
+      out.units[r * clusters + c] = make_int4(it.tm, it.tn, it.lo, it.hi | (it.flags << 24));
+    }
+  return out;
 }
 
 bool valid_desc(const b2g_gemm_desc* d) {
@@ -351,16 +478,17 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   const int64_t batch = d->batch;
   int bn = 256, ctas = 1;
   static const char* forced = std::getenv("B2G_TILE");
+  // Triangular NN operands take the plain engine with diagonal-block copies
+  // (no transform warps); other triangular layouts mask in the transform warps.
+  const bool tri_diag = d->op != B2G_OP_GEMM && !x3 && !d->trans_a && !d->trans_b;
   if (x3 || d->op != B2G_OP_GEMM) {
-    // Transform-warp variants (3xTF32 split, triangular masking): CTA-pair
-    // 256 x 256 units once there are at least two 128-row blocks, else one
-    // CTA with 128-wide tiles.
-    // Triangular ops stay on single-CTA 128-wide units: measured faster at
-    // N = 4096 (106 us vs 190 us for CTA pairs), whose transform warps mask
-    // twice the tile per K block.
+    // CTA-pair 256 x 256 units once there are at least two 128-row blocks,
+    // else one CTA with 128-wide tiles.  Triangular ops that still need the
+    // transform warps stay on single-CTA units (measured at N = 4096: 106 us
+    // vs 190 us for pairs, whose transform warps mask twice the tile).
     const bool force_single = forced && std::strncmp(forced, "single", 6) == 0;
     const bool force_pair = forced && std::strncmp(forced, "pair", 4) == 0;
-    if (d->m > kBlockM && !force_single && (x3 || force_pair)) {
+    if (d->m > kBlockM && !force_single && (x3 || tri_diag || force_pair)) {
       ctas = 2;
       bn = 256;
     } else {
@@ -426,6 +554,7 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   pl->b_mn_major = d->trans_b ? 0 : 1;
   pl->tma_store = (reinterpret_cast<uintptr_t>(d->c) % 16 == 0) && (d->ldc % 4 == 0) &&
                   (d->batch == 1 || d->stride_c % 4 == 0);
+  pl->tri_diag = tri_diag ? 1 : 0;
   const int64_t sa_batch = (d->stride_a == 0) ? 1 : batch;
   const int64_t sb_batch = (d->stride_b == 0) ? 1 : batch;
   pl->stage_a = tma_ok(d->a, d->lda, d->stride_a, sa_batch) ? 0 : 1;
@@ -435,6 +564,14 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
     ws += stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, sa_batch).bytes;
   if (pl->stage_b)
     ws += stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, sb_batch).bytes;
+  if (pl->tri_diag) {
+    ws += 2 * round_up(d->m * kTriDiagBlock * 4, 256);
+    const TriTable tt = build_tri_table(d, pl->block_m, pl->block_n, pl->tiles_m, pl->tiles_n,
+                                        pl->grid / ctas, pl->tma_store);
+    ws += round_up(static_cast<int64_t>(tt.units.size()) * sizeof(int4), 256);
+    ws += round_up(static_cast<int64_t>(tt.split_tiles.size()) * sizeof(int2), 256);
+    pl->work_units = static_cast<int64_t>(tt.units.size());
+  }
   pl->workspace_bytes = ws;
   return B2G_OK;
 }
@@ -479,6 +616,40 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     ws += g.bytes;
   }
 
+  float* adiag = nullptr;
+  float* bdiag = nullptr;
+  TriTable tri;
+  int4* table = nullptr;
+  if (pl.tri_diag) {
+    const int64_t nbytes = round_up(d->m * kTriDiagBlock * 4, 256);
+    adiag = reinterpret_cast<float*>(ws);
+    bdiag = reinterpret_cast<float*>(ws + nbytes);
+    ws += 2 * nbytes;
+    // Unit table (longest-first, split long tiles) followed by the split
+    // tiles' coordinates: one upload, then one pre-pass launch.
+    tri = build_tri_table(d, pl.block_m, pl.block_n, pl.tiles_m, pl.tiles_n,
+                          pl.grid / pl.cluster_ctas, pl.tma_store);
+    const int64_t tbytes = static_cast<int64_t>(tri.units.size()) * sizeof(int4);
+    const int64_t zbytes = static_cast<int64_t>(tri.split_tiles.size()) * sizeof(int2);
+    std::vector<char> host(round_up(tbytes, 256) + zbytes);
+    std::memcpy(host.data(), tri.units.data(), tbytes);
+    if (zbytes) std::memcpy(host.data() + round_up(tbytes, 256), tri.split_tiles.data(), zbytes);
+    table = reinterpret_cast<int4*>(ws);
+    const int2* split_list = reinterpret_cast<const int2*>(ws + round_up(tbytes, 256));
+    ws += round_up(tbytes, 256) + round_up(zbytes, 256);
+    if (cudaMemcpyAsync(table, host.data(), host.size(), cudaMemcpyHostToDevice, stream) !=
+        cudaSuccess)
+      return B2G_ERR_LAUNCH;
+    const int n_split = static_cast<int>(tri.split_tiles.size());
+    const int64_t diag_blocks = cdiv(d->m, kTriDiagBlock) * (kTriDiagBlock / kTriDiagRows);
+    const int64_t zero_blocks = static_cast<int64_t>(n_split) * cdiv(pl.block_m, kTriDiagRows);
+    dim3 grid(static_cast<unsigned>(std::max(diag_blocks, zero_blocks)), n_split ? 3 : 2);
+    tri_prepare_kernel<<<grid, 256, 0, stream>>>(a, lda, b, ldb, d->m,
+                                                  d->op == B2G_OP_TRI_UPPER, adiag, bdiag, d->c,
+                                                  d->ldc, split_list, n_split, pl.block_m,
+                                                  pl.block_n);
+  }
+
   EngineParams p;
   std::memset(&p, 0, sizeof(p));
   p.M = static_cast<int>(d->m);
@@ -507,6 +678,9 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.wait_limit_ns = wait_limit_ns();
   p.inject_stall = take_injected_stall();
   p.tri_sorted = (p.tri != kTriNone && pl.block_m == pl.block_n) ? 1 : 0;
+  p.tri_diag = pl.tri_diag;
+  p.unit_table = table;
+  p.diag_oob_row = static_cast<int>(d->m);
   p.err = err_word;
 
   if (p.atomic_out) {
@@ -544,36 +718,40 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   } else {
     mc = ma;   // unused by the kernel
   }
+  CUtensorMap mad = ma, mbd = ma;   // diagonal-block copies (triangular NN only)
+  if (pl.tri_diag) {
+    const int bcols = std::min(pl.block_n, 256) / pl.cluster_ctas;
+    if (bcols != kTriDiagBlock ||
+        !make_map(&mad, adiag, kTriDiagBlock, d->m, 1, kTriDiagBlock, 0, kBlockK, kBlockM, false) ||
+        !make_map_grouped(&mbd, bdiag, kTriDiagBlock, d->m, 1, kTriDiagBlock, 0,
+                          kTriDiagBlock / 32))
+      return B2G_ERR_UNSUPPORTED;
+  }
 
   const bool a_mn = pl.a_mn_major, b_mn = pl.b_mn_major;
   const bool x3 = d->precision == B2G_PREC_3XTF32;
-  const bool tri = p.tri != kTriNone;
+  const bool tri_xf = p.tri != kTriNone && !pl.tri_diag;   // triangular via transform warps
   const int grid = pl.grid;
+  const CUtensorMap maps[5] = {ma, mb, mc, mad, mbd};
   if (x3 && pl.cluster_ctas == 2)
-    return launch_majors<256, 3, true, true, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+    return launch_majors<256, 3, true, true, true>(a_mn, b_mn, maps, p, grid, stream);
   if (x3)
-    return launch_majors<128, 3, true, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
-#ifdef B2G_EXP_TRI_NOXF
-  if (tri && pl.cluster_ctas == 2)
-    return launch_majors<256, 6, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
-  if (tri)
-    return launch_majors<128, 6, false, false, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
-#endif
-  if (tri && pl.cluster_ctas == 2)
-    return launch_majors<256, 6, false, true, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+    return launch_majors<128, 3, true, true, false>(a_mn, b_mn, maps, p, grid, stream);
+  if (tri_xf && pl.cluster_ctas == 2)
+    return launch_majors<256, 6, false, true, true>(a_mn, b_mn, maps, p, grid, stream);
+  if (tri_xf)
+    return launch_majors<128, 6, false, true, false>(a_mn, b_mn, maps, p, grid, stream);
   if (pl.cluster_ctas == 2) {
     if (pl.block_n == 512)
-      return launch_majors<512, 4, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+      return launch_majors<512, 4, false, false, true>(a_mn, b_mn, maps, p, grid, stream);
     if (pl.block_n == 256)
       return launch_majors<256, B2G_PAIR256_STAGES, false, false, true, B2G_PAIR256_EPIG>(
-          a_mn, b_mn, ma, mb, mc, p, grid, stream);
-    return launch_majors<128, 8, false, false, true>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+          a_mn, b_mn, maps, p, grid, stream);
+    return launch_majors<128, 8, false, false, true>(a_mn, b_mn, maps, p, grid, stream);
   }
   if (pl.block_n == 256)
-    return launch_majors<256, 4, false, false, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
-  if (tri)
-    return launch_majors<128, 6, false, true, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
-  return launch_majors<128, 6, false, false, false>(a_mn, b_mn, ma, mb, mc, p, grid, stream);
+    return launch_majors<256, 4, false, false, false>(a_mn, b_mn, maps, p, grid, stream);
+  return launch_majors<128, 6, false, false, false>(a_mn, b_mn, maps, p, grid, stream);
 }
 
 extern "C" int b2g_gemm(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {

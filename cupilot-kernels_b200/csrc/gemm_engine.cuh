@@ -63,12 +63,20 @@ struct EngineParams {
   long long wait_limit_ns;     // bound on every mbarrier wait
   int inject_stall;            // test hook: the MMA warp never signals tmem_full
   int tri_sorted;              // triangular op on square units: longest K range first
+  int tri_diag;                // triangular inputs masked through diagonal-block copies
+  const int4* unit_table;      // if set: unit w is {tm, tn, kb_lo, kb_hi | flags << 24}
+  int diag_oob_row;            // a K row past every operand row (zero-filled by TMA)
   int* err;
 };
 
 struct WorkUnit {
   int b, tm, tn, kb_lo, kb_hi;
+  int accumulate;   // reduce-add into C (a K piece of a split tile)
+  int skip;         // padding entry of a unit table: no work, no output
 };
+
+// Unit-table flags (bits 24.. of .w).
+enum : int { kUnitAccumulate = 1, kUnitSkip = 2 };
 
 // Map a linear work-unit index to (batch, tile, K range).  Tiles are
 // rasterised in groups of group_m tile-rows so CTAs that run together share
@@ -109,6 +117,23 @@ __host__ __device__ inline void decode_tri_sorted(const EngineParams& p, long lo
 
 __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long w) {
   WorkUnit u;
+  u.accumulate = 0;
+  u.skip = 0;
+  if (p.unit_table != nullptr) {
+#ifdef __CUDA_ARCH__
+    const int4 e = __ldg(p.unit_table + w);
+#else
+    const int4 e = p.unit_table[w];
+#endif
+    u.b = 0;
+    u.tm = e.x;
+    u.tn = e.y;
+    u.kb_lo = e.z;
+    u.kb_hi = e.w & 0xFFFFFF;
+    u.accumulate = (e.w >> 24) & kUnitAccumulate;
+    u.skip = ((e.w >> 24) & kUnitSkip) ? 1 : 0;
+    return u;
+  }
   const int split = static_cast<int>(w % p.splits);
   const long long t = w / p.splits;
   const long long per_batch = static_cast<long long>(p.tiles_m) * p.tiles_n;
@@ -403,7 +428,8 @@ __device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtenso
 template <int G>
 __device__ __forceinline__ void store_group_tma(const EngineParams& p, const CUtensorMap* map_c,
                                                 float* stg, uint32_t (&r)[G][32], int ng, int b,
-                                                int row0, const int (&col0)[G], int lane) {
+                                                int row0, const int (&col0)[G], int lane,
+                                                int accumulate) {
   const int row = row0 + lane;
   if (p.tri != kTriNone) {
 #pragma unroll
@@ -433,7 +459,7 @@ __device__ __forceinline__ void store_group_tma(const EngineParams& p, const CUt
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       if (g < ng) {
-        if (p.atomic_out)
+        if (p.atomic_out || accumulate)
           ptx::tma_reduce_add_3d(map_c, stg + g * 32 * 32, col0[g], row0, b);
         else
           ptx::tma_store_3d(map_c, stg + g * 32 * 32, col0[g], row0, b);
@@ -447,7 +473,9 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR,
 __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>::kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_b,
-                     const __grid_constant__ CUtensorMap map_c, const EngineParams p) {
+                     const __grid_constant__ CUtensorMap map_c,
+                     const __grid_constant__ CUtensorMap map_ad,
+                     const __grid_constant__ CUtensorMap map_bd, const EngineParams p) {
   using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -488,6 +516,10 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
     ptx::prefetch_tmap(&map_a);
     ptx::prefetch_tmap(&map_b);
     if (p.tma_store) ptx::prefetch_tmap(&map_c);
+    if (p.tri_diag) {
+      ptx::prefetch_tmap(&map_ad);
+      ptx::prefetch_tmap(&map_bd);
+    }
   }
   if (warp == 1) {
     if (PAIR) {
@@ -551,7 +583,37 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
             else
               ptx::tma_load_4d(dst, map, &full[s], 0, k0, g0, c3);
           };
-          if (!A_MN) {
+          // Triangular operands through diagonal-block copies: a K block that
+          // crosses this CTA's diagonal block comes from the masked copy, one
+          // wholly in the masked triangle from outside every operand (TMA
+          // fills zeros), any other from the operand itself.
+          bool a_done = false, b_done = false;
+          if (!A_MN && !XF && p.tri_diag) {
+            const bool use_diag = p.tri == kTriUpper ? (k0 < m_cta + kBlockM)
+                                                     : (k0 + kBlockK - 1 >= m_cta);
+            if (use_diag) {
+              load(sa, &map_ad, k0 - m_cta, m_cta, 0);   // x < 0 or >= 128: zero fill
+              a_done = true;
+            }
+          }
+          if (B_MN && !XF && p.tri_diag && Cfg::kNSub == 1) {
+            const int c0 = n_cta;
+            int y = -1;
+            if (p.tri == kTriUpper) {
+              if (k0 >= c0) y = k0 < c0 + Cfg::kSubCols ? k0 : p.diag_oob_row;
+            } else {
+              if (k0 < c0 + Cfg::kSubCols) y = k0 >= c0 ? k0 : -kBlockK;
+            }
+            if (y != -1) {
+              if (PAIR && !XF)
+                ptx::tma_load_4d_pair(sb, &map_bd, full_leader + s * 8, 0, y, 0, 0);
+              else
+                ptx::tma_load_4d(sb, &map_bd, &full[s], 0, y, 0, 0);
+              b_done = true;
+            }
+          }
+          if (a_done) {
+          } else if (!A_MN) {
             load(sa, &map_a, k0, m_cta, ab);
           } else if (p.a_grouped) {
             load_grouped(sa, &map_a, m_cta / 32, ab);
@@ -561,7 +623,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
               load(sa + j * kBlockK * kSwRowBytes, &map_a, m_cta + 32 * j, k0, ab);
           }
 #pragma unroll
-          for (int j = 0; j < Cfg::kNSub; ++j) {
+          for (int j = 0; j < Cfg::kNSub && !b_done; ++j) {
             uint8_t* sbj = sb + j * Cfg::kBSubBytes;
             const int nj = n_cta + j * Cfg::kMmaN;
             if (!B_MN) {
@@ -700,9 +762,10 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       const WorkUnit u = decode_unit(p, w);
       const int row0 = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM + quad * 32;
       const int n0 = u.tn * BN;
+      if (u.skip) continue;
       if (u.kb_lo >= u.kb_hi) {
         // Structurally zero tile (or K == 0): write zeros unless accumulating.
-        if (!p.atomic_out && row0 < p.M) {
+        if (!p.atomic_out && !u.accumulate && row0 < p.M) {
           float* cb = p.C + static_cast<long long>(u.b) * p.stride_c;
           for (int it = 0; it < 8 * (BN / 64); ++it) {
             const int r_local = (it & 7) * 4 + (lane >> 3);
@@ -755,7 +818,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
 #pragma unroll
             for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[g][i]));
           if (g0 + G >= mine) release();                      // every TMEM read is done
-          store_group_tma<G>(p, &map_c, stg, r, ng, u.b, row0, col0, lane);
+          store_group_tma<G>(p, &map_c, stg, r, ng, u.b, row0, col0, lane, u.accumulate);
         }
       } else if (row0 < p.M && half < nch) {
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;

@@ -40,7 +40,7 @@ def test_version_and_status_strings(capi):
 def test_struct_layout_matches_header(capi):
     # 2 x int32 + 4 x int64 + 3 x (ptr, int64, int64, int32->padded) ... checked by size.
     assert ctypes.sizeof(capi.GemmDesc) == 8 + 32 + 3 * 32 - 8 + 16
-    assert ctypes.sizeof(capi.GemmPlan) == 15 * 4 + 4 + 16
+    assert ctypes.sizeof(capi.GemmPlan) == 16 * 4 + 16
 
 
 ALIGNED = 1 << 20   # a fake 16-byte-aligned device address: planning never dereferences
@@ -94,7 +94,12 @@ def test_plan_large_k_splits(capi):
 
 def test_plan_triangular_never_splits(capi):
     p = _plan(capi, 256, 256, 256, op=capi.OP_TRI_UPPER)
-    assert p.splits == 1 and p.cluster_ctas == 1
+    assert p.splits == 1 and p.cluster_ctas == 2 and p.tri_diag == 1
+    # diagonal-block copies of A and B (2 x 256 rows x 128 fp32) plus the unit table
+    assert p.workspace_bytes >= 2 * 256 * 128 * 4
+    assert p.work_units % (p.grid // 2) == 0   # table rows of one entry per CTA pair
+    q = _plan(capi, 256, 256, 256, op=capi.OP_TRI_LOWER, trans_a=1)
+    assert q.tri_diag == 0 and q.cluster_ctas == 1
 
 
 def test_plan_irregular_stages_unaligned_operands(capi):
