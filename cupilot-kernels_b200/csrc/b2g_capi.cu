@@ -15,7 +15,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <queue>
 #include <vector>
 
@@ -352,7 +354,7 @@ TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int t
   for (const WorkUnit& u : tiles) {
     const int len = u.kb_hi - u.kb_lo;
     if (len == 0) {
-      items.push_back({u.tm, u.tn, 0, 0, 0, 2});   // zero tile: epilogue work only
+      items.push_back({u.tm, u.tn, 0, 0, 0, 3});   // zero tile: epilogue stores only
       continue;
     }
     const int np = static_cast<int>(cdiv(len, lmax));
@@ -385,6 +387,25 @@ TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int t
       out.units[r * clusters + c] = make_int4(it.tm, it.tn, it.lo, it.hi | (it.flags << 24));
     }
   return out;
+}
+
+// build_tri_table memoised on everything it depends on (shape, triangle,
+// tiling, cluster count, whether K pieces may reduce-add): repeated calls of
+// one shape reuse the table instead of re-sorting it on the host.
+const TriTable& cached_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int tiles_m,
+                                 int tiles_n, int clusters, bool allow_split) {
+  using Key = std::tuple<int64_t, int64_t, int, int, int, int, int, int, int>;
+  static std::mutex mu;
+  static std::map<Key, TriTable> cache;
+  const Key key{d->m, d->k, d->op, block_m, block_n, tiles_m, tiles_n, clusters, allow_split};
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it == cache.end()) {
+    if (cache.size() > 64) cache.clear();
+    it = cache.emplace(key, build_tri_table(d, block_m, block_n, tiles_m, tiles_n, clusters,
+                                            allow_split)).first;
+  }
+  return it->second;
 }
 
 bool valid_desc(const b2g_gemm_desc* d) {
@@ -566,8 +587,8 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
     ws += stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, sb_batch).bytes;
   if (pl->tri_diag) {
     ws += 2 * round_up(d->m * kTriDiagBlock * 4, 256);
-    const TriTable tt = build_tri_table(d, pl->block_m, pl->block_n, pl->tiles_m, pl->tiles_n,
-                                        pl->grid / ctas, pl->tma_store);
+    const TriTable& tt = cached_tri_table(d, pl->block_m, pl->block_n, pl->tiles_m,
+                                          pl->tiles_n, pl->grid / ctas, pl->tma_store);
     ws += round_up(static_cast<int64_t>(tt.units.size()) * sizeof(int4), 256);
     ws += round_up(static_cast<int64_t>(tt.split_tiles.size()) * sizeof(int2), 256);
     pl->work_units = static_cast<int64_t>(tt.units.size());
@@ -618,7 +639,6 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
 
   float* adiag = nullptr;
   float* bdiag = nullptr;
-  TriTable tri;
   int4* table = nullptr;
   if (pl.tri_diag) {
     const int64_t nbytes = round_up(d->m * kTriDiagBlock * 4, 256);
@@ -627,8 +647,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     ws += 2 * nbytes;
     // Unit table (longest-first, split long tiles) followed by the split
     // tiles' coordinates: one upload, then one pre-pass launch.
-    tri = build_tri_table(d, pl.block_m, pl.block_n, pl.tiles_m, pl.tiles_n,
-                          pl.grid / pl.cluster_ctas, pl.tma_store);
+    const TriTable& tri = cached_tri_table(d, pl.block_m, pl.block_n, pl.tiles_m, pl.tiles_n,
+                                           pl.grid / pl.cluster_ctas, pl.tma_store);
     const int64_t tbytes = static_cast<int64_t>(tri.units.size()) * sizeof(int4);
     const int64_t zbytes = static_cast<int64_t>(tri.split_tiles.size()) * sizeof(int2);
     std::vector<char> host(round_up(tbytes, 256) + zbytes);

@@ -763,6 +763,25 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
       const int row0 = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM + quad * 32;
       const int n0 = u.tn * BN;
       if (u.skip) continue;
+      if (u.kb_lo >= u.kb_hi && p.tma_store) {
+        // Structurally zero tile (or K == 0): TMA-store a zeroed staging box
+        // over this warp's chunks, unless the tile only accumulates.
+        if (!p.atomic_out && !u.accumulate && row0 < p.M) {
+          if (lane == 0) ptx::bulk_wait_read<0>();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(stg + lane * 32 + j * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            for (int ch = half; ch * 32 < BN && n0 + ch * 32 < p.N; ch += 2)
+              ptx::tma_store_3d(&map_c, stg, n0 + ch * 32, row0, u.b);
+            ptx::bulk_commit();
+          }
+        }
+        continue;
+      }
       if (u.kb_lo >= u.kb_hi) {
         // Structurally zero tile (or K == 0): write zeros unless accumulating.
         if (!p.atomic_out && !u.accumulate && row0 < p.M) {
