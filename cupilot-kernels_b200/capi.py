@@ -45,6 +45,7 @@ class GemmPlan(C.Structure):
         ("stage_a", C.c_int32), ("stage_b", C.c_int32),
         ("a_mn_major", C.c_int32), ("b_mn_major", C.c_int32),
         ("cluster_ctas", C.c_int32), ("tma_store", C.c_int32), ("tri_diag", C.c_int32),
+        ("x3_split", C.c_int32),
         ("work_units", C.c_int64), ("workspace_bytes", C.c_int64),
     ]
 

@@ -220,6 +220,26 @@ __global__ void __launch_bounds__(256) tri_prepare_kernel(
   }
 }
 
+// 3xTF32 pre-split: dst[b][r][c] = x - (x with its low 13 mantissa bits
+// cleared), x = src[b*sstride + r*sld + c]; the tensor core truncates the
+// original operand to its TF32 "hi" part itself.
+__global__ void __launch_bounds__(256) split_lo_kernel(const float* __restrict__ src,
+                                                       float* __restrict__ dst, int64_t rows,
+                                                       int64_t cols, int64_t sld, int64_t sstride,
+                                                       int64_t dld, int64_t dstride,
+                                                       int64_t batch) {
+  const int64_t total = batch * rows;
+  for (int64_t rr = blockIdx.x; rr < total; rr += gridDim.x) {
+    const int64_t b = rr / rows, r = rr - b * rows;
+    const float* s = src + b * sstride + r * sld;
+    float* d = dst + b * dstride + r * dld;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+      const float x = __ldg(s + c);
+      d[c] = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- row scale
 // out[i][j] = d[i] * B[i][j]; 16-byte loads/stores when the layout allows.
 __global__ void __launch_bounds__(256) rowscale_vec_kernel(const float* __restrict__ d,
@@ -502,6 +522,9 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   // Triangular NN operands take the plain engine with diagonal-block copies
   // (no transform warps); other triangular layouts mask in the transform warps.
   const bool tri_diag = d->op != B2G_OP_GEMM && !x3 && !d->trans_a && !d->trans_b;
+  // 3xTF32 on plain GEMMs: lo parts pre-split into workspace, loaded by TMA;
+  // triangular 3xTF32 masks and splits in the (single-CTA) transform warps.
+  const bool x3_split = x3 && d->op == B2G_OP_GEMM;
   if (x3 || d->op != B2G_OP_GEMM) {
     // CTA-pair 256 x 256 units once there are at least two 128-row blocks,
     // else one CTA with 128-wide tiles.  Triangular ops that still need the
@@ -509,7 +532,7 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
     // vs 190 us for pairs, whose transform warps mask twice the tile).
     const bool force_single = forced && std::strncmp(forced, "single", 6) == 0;
     const bool force_pair = forced && std::strncmp(forced, "pair", 4) == 0;
-    if (d->m > kBlockM && !force_single && (x3 || tri_diag || force_pair)) {
+    if (d->m > kBlockM && !force_single && (x3_split || tri_diag || force_pair)) {
       ctas = 2;
       bn = 256;
     } else {
@@ -576,6 +599,7 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   pl->tma_store = (reinterpret_cast<uintptr_t>(d->c) % 16 == 0) && (d->ldc % 4 == 0) &&
                   (d->batch == 1 || d->stride_c % 4 == 0);
   pl->tri_diag = tri_diag ? 1 : 0;
+  pl->x3_split = x3_split ? 1 : 0;
   const int64_t sa_batch = (d->stride_a == 0) ? 1 : batch;
   const int64_t sb_batch = (d->stride_b == 0) ? 1 : batch;
   pl->stage_a = tma_ok(d->a, d->lda, d->stride_a, sa_batch) ? 0 : 1;
@@ -585,6 +609,10 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
     ws += stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, sa_batch).bytes;
   if (pl->stage_b)
     ws += stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, sb_batch).bytes;
+  if (pl->x3_split) {
+    ws += stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, sa_batch).bytes;
+    ws += stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, sb_batch).bytes;
+  }
   if (pl->tri_diag) {
     ws += 2 * round_up(d->m * kTriDiagBlock * 4, 256);
     const TriTable& tt = cached_tri_table(d, pl->block_m, pl->block_n, pl->tiles_m,
@@ -637,6 +665,28 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     ws += g.bytes;
   }
 
+  // 3xTF32 pre-split: lo copies of A and B at a 16-byte pitch.
+  const float* alo = nullptr;
+  const float* blo = nullptr;
+  int64_t ldalo = 0, ldblo = 0, salo = 0, sblo = 0;
+  if (pl.x3_split && d->k > 0) {
+    Stage ga = stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, a_batch);
+    float* da = reinterpret_cast<float*>(ws);
+    ws += ga.bytes;
+    split_lo_kernel<<<static_cast<int>(std::min<int64_t>(ga.rows * ga.nbatch, 65535)), 256, 0,
+                      stream>>>(a, da, ga.rows, ga.cols, lda, sa, ga.pitch, ga.bstride, ga.nbatch);
+    Stage gb = stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, b_batch);
+    float* db = reinterpret_cast<float*>(ws);
+    ws += gb.bytes;
+    split_lo_kernel<<<static_cast<int>(std::min<int64_t>(gb.rows * gb.nbatch, 65535)), 256, 0,
+                      stream>>>(b, db, gb.rows, gb.cols, ldb, sb, gb.pitch, gb.bstride, gb.nbatch);
+    alo = da;
+    blo = db;
+    ldalo = ga.pitch;
+    ldblo = gb.pitch;
+    salo = a_batch > 1 ? ga.bstride : 0;
+    sblo = b_batch > 1 ? gb.bstride : 0;
+  }
   float* adiag = nullptr;
   float* bdiag = nullptr;
   int4* table = nullptr;
@@ -738,7 +788,25 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   } else {
     mc = ma;   // unused by the kernel
   }
-  CUtensorMap mad = ma, mbd = ma;   // diagonal-block copies (triangular NN only)
+  CUtensorMap mad = ma, mbd = ma;   // diagonal-block copies (triangular) or lo parts (3xTF32)
+  if (pl.x3_split && alo) {
+    // The lo copies are laid out like the operands (same majorness and box),
+    // so they take the same map geometry; a grouped A/B implies a grouped copy.
+    if (!pl.a_mn_major)
+      ok = make_map(&mad, alo, k_ext, d->m, a_batch, ldalo, salo, kBlockK, kBlockM, false);
+    else if (p.a_grouped)
+      ok = make_map_grouped(&mad, alo, d->m, k_ext, a_batch, ldalo, salo, kBlockM / 32);
+    else
+      ok = make_map(&mad, alo, d->m, k_ext, a_batch, ldalo, salo, 32, kBlockK, true);
+    if (!ok) return B2G_ERR_UNSUPPORTED;
+    if (!pl.b_mn_major)
+      ok = make_map(&mbd, blo, k_ext, d->n, b_batch, ldblo, sblo, kBlockK, bn_cta, false);
+    else if (p.b_grouped)
+      ok = make_map_grouped(&mbd, blo, d->n, k_ext, b_batch, ldblo, sblo, bn_cta / 32);
+    else
+      ok = make_map(&mbd, blo, d->n, k_ext, b_batch, ldblo, sblo, 32, kBlockK, true);
+    if (!ok) return B2G_ERR_UNSUPPORTED;
+  }
   if (pl.tri_diag) {
     const int bcols = std::min(pl.block_n, 256) / pl.cluster_ctas;
     if (bcols != kTriDiagBlock ||
@@ -753,9 +821,11 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   const bool tri_xf = p.tri != kTriNone && !pl.tri_diag;   // triangular via transform warps
   const int grid = pl.grid;
   const CUtensorMap maps[5] = {ma, mb, mc, mad, mbd};
-  if (x3 && pl.cluster_ctas == 2)
-    return launch_majors<256, 3, true, true, true>(a_mn, b_mn, maps, p, grid, stream);
-  if (x3)
+  if (x3 && pl.x3_split && pl.cluster_ctas == 2)
+    return launch_majors<256, 3, true, false, true>(a_mn, b_mn, maps, p, grid, stream);
+  if (x3 && pl.x3_split)
+    return launch_majors<128, 3, true, false, false>(a_mn, b_mn, maps, p, grid, stream);
+  if (x3)   // triangular 3xTF32: masking and split in the transform warps
     return launch_majors<128, 3, true, true, false>(a_mn, b_mn, maps, p, grid, stream);
   if (tri_xf && pl.cluster_ctas == 2)
     return launch_majors<256, 6, false, true, true>(a_mn, b_mn, maps, p, grid, stream);

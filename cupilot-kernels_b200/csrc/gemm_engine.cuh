@@ -194,7 +194,8 @@ struct EngineCfg {
   static constexpr int kABytes = kBlockM * kBlockK * 4;
   static constexpr int kBSubBytes = kSubCols * kBlockK * 4;
   static constexpr int kBBytes = kBnCta * kBlockK * 4;
-  static constexpr int kStageTx = kABytes + kBBytes;        // bytes per CTA per stage
+  static constexpr bool kPreSplit = X3 && !XF;               // lo parts loaded by TMA
+  static constexpr int kStageTx = (kABytes + kBBytes) * (kPreSplit ? 2 : 1);   // per CTA
   static constexpr int kOperandBufs = X3 ? 2 : 1;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = STAGES * kABytes;
@@ -217,7 +218,6 @@ struct EngineCfg {
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(BN % 64 == 0 && BN <= (PAIR ? 512 : 256), "BN");
-  static_assert(!X3 || XF, "the 3xTF32 split runs in the transform warps");
   static_assert(!(PAIR && XF) || kNSub == 1, "transform warps handle one B sub-tile");
 };
 
@@ -610,6 +610,35 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
               else
                 ptx::tma_load_4d(sb, &map_bd, &full[s], 0, y, 0, 0);
               b_done = true;
+            }
+          }
+          if (X3 && !XF) {
+            // 3xTF32 with pre-split operands: the lo parts come from their own
+            // copies (map_ad / map_bd), at the same coordinates as A and B.
+            uint8_t* sal = smem + Cfg::kOffALo + s * Cfg::kABytes;
+            uint8_t* sbl = smem + Cfg::kOffBLo + s * Cfg::kBBytes;
+            if (!A_MN) {
+              load(sal, &map_ad, k0, m_cta, ab);
+            } else if (p.a_grouped) {
+              load_grouped(sal, &map_ad, m_cta / 32, ab);
+            } else {
+#pragma unroll
+              for (int j = 0; j < kBlockM / 32; ++j)
+                load(sal + j * kBlockK * kSwRowBytes, &map_ad, m_cta + 32 * j, k0, ab);
+            }
+#pragma unroll
+            for (int j = 0; j < Cfg::kNSub; ++j) {
+              uint8_t* sblj = sbl + j * Cfg::kBSubBytes;
+              const int nj = n_cta + j * Cfg::kMmaN;
+              if (!B_MN) {
+                load(sblj, &map_bd, k0, nj, bb);
+              } else if (p.b_grouped) {
+                load_grouped(sblj, &map_bd, nj / 32, bb);
+              } else {
+#pragma unroll
+                for (int g = 0; g < Cfg::kSubCols / 32; ++g)
+                  load(sblj + g * kBlockK * kSwRowBytes, &map_bd, nj + 32 * g, k0, bb);
+              }
             }
           }
           if (a_done) {

@@ -111,6 +111,7 @@ typedef struct b2g_gemm_plan {
   int32_t cluster_ctas;         /* 2: a CTA pair computes each 256-row unit (tcgen05 cta_group::2) */
   int32_t tma_store;            /* 1: C written by TMA tensor stores (C rows 16-byte aligned) */
   int32_t tri_diag;             /* 1: triangular inputs masked through diagonal-block copies in workspace */
+  int32_t x3_split;             /* 1: 3xTF32 lo parts pre-split into workspace (plain GEMMs) */
   int64_t work_units;
   int64_t workspace_bytes;
 } b2g_gemm_plan;

@@ -40,7 +40,7 @@ def test_version_and_status_strings(capi):
 def test_struct_layout_matches_header(capi):
     # 2 x int32 + 4 x int64 + 3 x (ptr, int64, int64, int32->padded) ... checked by size.
     assert ctypes.sizeof(capi.GemmDesc) == 8 + 32 + 3 * 32 - 8 + 16
-    assert ctypes.sizeof(capi.GemmPlan) == 16 * 4 + 16
+    assert ctypes.sizeof(capi.GemmPlan) == 17 * 4 + 4 + 16
 
 
 ALIGNED = 1 << 20   # a fake 16-byte-aligned device address: planning never dereferences
@@ -70,6 +70,11 @@ def test_plan_transposes_set_majorness(capi):
     assert p.a_mn_major == 1 and p.b_mn_major == 0
     # 32 units of 256 x 256 fill 64 SMs: K is split in two to fill 128.
     assert p.cluster_ctas == 2 and p.block_n == 256 and p.splits == 2 and p.grid == 128
+
+
+def test_plan_triangular_3xtf32_uses_the_transform_variant(capi):
+    p = _plan(capi, 300, 300, 300, op=capi.OP_TRI_UPPER, precision=capi.PREC_3XTF32)
+    assert p.cluster_ctas == 1 and p.block_n == 128 and p.tri_diag == 0 and p.x3_split == 0
 
 
 def test_plan_grid_is_even_for_pairs(capi):
@@ -120,7 +125,8 @@ def test_plan_misaligned_base_pointer_is_staged(capi):
 
 def test_plan_3xtf32_uses_narrow_tiles(capi):
     p = _plan(capi, 2048, 2048, 2048, precision=capi.PREC_3XTF32)
-    assert p.block_n == 256 and p.stages == 3 and p.cluster_ctas == 2
+    assert p.block_n == 256 and p.stages == 3 and p.cluster_ctas == 2 and p.x3_split == 1
+    assert p.workspace_bytes == 2 * 2048 * 2048 * 4      # lo parts of A and B
 
 
 def test_plan_batched(capi):
