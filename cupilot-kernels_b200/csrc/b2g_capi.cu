@@ -30,6 +30,9 @@
 #ifndef B2G_PAIR256_EPIG
 #define B2G_PAIR256_EPIG 1     // accumulator chunks per epilogue store group
 #endif
+#ifndef B2G_PAIR256_EPIW
+#define B2G_PAIR256_EPIW 8     // epilogue warps of the CTA-pair 256-wide engine
+#endif
 
 namespace b2g {
 namespace {
@@ -163,7 +166,9 @@ bool make_map_grouped(CUtensorMap* map, const float* base, int64_t mn, int64_t k
 }
 
 // ---------------------------------------------------------------- staging copy
-// dst[b][r][c] = src[b*sstride + r*sld + c], dst pitch dld (multiple of 4).
+// dst[b][r][c] = src[b*sstride + r*sld + c] for c < cols, 0 for cols <= c
+// < dld (the pitch, a multiple of 4; a multiple of 32 for MN-major
+// operands, whose zero-padded columns let the loads use 32-wide groups).
 __global__ void pitch_copy_kernel(const float* __restrict__ src, float* __restrict__ dst,
                                   int64_t rows, int64_t cols, int64_t sld, int64_t sstride,
                                   int64_t dld, int64_t dstride, int64_t batch) {
@@ -172,7 +177,7 @@ __global__ void pitch_copy_kernel(const float* __restrict__ src, float* __restri
     const int64_t b = rr / rows, r = rr - b * rows;
     const float* s = src + b * sstride + r * sld;
     float* d = dst + b * dstride + r * dld;
-    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) d[c] = __ldg(s + c);
+    for (int64_t c = threadIdx.x; c < dld; c += blockDim.x) d[c] = c < cols ? __ldg(s + c) : 0.f;
   }
 }
 
@@ -233,8 +238,8 @@ __global__ void __launch_bounds__(256) split_lo_kernel(const float* __restrict__
     const int64_t b = rr / rows, r = rr - b * rows;
     const float* s = src + b * sstride + r * sld;
     float* d = dst + b * dstride + r * dld;
-    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
-      const float x = __ldg(s + c);
+    for (int64_t c = threadIdx.x; c < dld; c += blockDim.x) {
+      const float x = c < cols ? __ldg(s + c) : 0.f;
       d[c] = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
     }
   }
@@ -285,12 +290,13 @@ __global__ void rowscale_scalar_kernel(const float* __restrict__ d, const float*
 }
 
 // ---------------------------------------------------------------- engine instantiations
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG>
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG,
+          int EPIW>
 int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
                   const CUtensorMap& mad, const CUtensorMap& mbd, const EngineParams& p, int grid,
                   cudaStream_t stream) {
-  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>;
-  auto kern = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>;
+  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG, EPIW>;
+  auto kern = gemm_tf32_kernel<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG, EPIW>;
   static thread_local int configured_dev = -1;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -319,19 +325,19 @@ int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
   return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
 }
 
-template <int BN, int STAGES, bool X3, bool XF, bool PAIR, int EPIG = 1>
+template <int BN, int STAGES, bool X3, bool XF, bool PAIR, int EPIG = 1, int EPIW = 8>
 int launch_majors(bool a_mn, bool b_mn, const CUtensorMap (&m)[5], const EngineParams& p,
                   int grid, cudaStream_t st) {
   if (!a_mn && !b_mn)
-    return launch_engine<BN, STAGES, false, false, X3, XF, PAIR, EPIG>(m[0], m[1], m[2], m[3],
+    return launch_engine<BN, STAGES, false, false, X3, XF, PAIR, EPIG, EPIW>(m[0], m[1], m[2], m[3],
                                                                         m[4], p, grid, st);
   if (!a_mn && b_mn)
-    return launch_engine<BN, STAGES, false, true, X3, XF, PAIR, EPIG>(m[0], m[1], m[2], m[3],
+    return launch_engine<BN, STAGES, false, true, X3, XF, PAIR, EPIG, EPIW>(m[0], m[1], m[2], m[3],
                                                                        m[4], p, grid, st);
   if (a_mn && !b_mn)
-    return launch_engine<BN, STAGES, true, false, X3, XF, PAIR, EPIG>(m[0], m[1], m[2], m[3],
+    return launch_engine<BN, STAGES, true, false, X3, XF, PAIR, EPIG, EPIW>(m[0], m[1], m[2], m[3],
                                                                        m[4], p, grid, st);
-  return launch_engine<BN, STAGES, true, true, X3, XF, PAIR, EPIG>(m[0], m[1], m[2], m[3], m[4],
+  return launch_engine<BN, STAGES, true, true, X3, XF, PAIR, EPIG, EPIW>(m[0], m[1], m[2], m[3], m[4],
                                                                     p, grid, st);
 }
 
@@ -462,11 +468,11 @@ bool tma_ok(const float* p, int64_t ld, int64_t stride, int64_t batch) {
 struct Stage {
   int64_t rows, cols, pitch, bstride, nbatch, bytes;
 };
-Stage stage_geom(int64_t rows, int64_t cols, int64_t nbatch) {
+Stage stage_geom(int64_t rows, int64_t cols, int64_t nbatch, int64_t align = 4) {
   Stage s;
   s.rows = rows;
   s.cols = cols;
-  s.pitch = round_up(std::max<int64_t>(cols, 1), 4);
+  s.pitch = round_up(std::max<int64_t>(cols, 1), align);
   s.bstride = s.pitch * rows;
   s.nbatch = nbatch;
   s.bytes = round_up(s.bstride * nbatch * 4, 256);
@@ -606,12 +612,16 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   pl->stage_b = tma_ok(d->b, d->ldb, d->stride_b, sb_batch) ? 0 : 1;
   int64_t ws = 0;
   if (pl->stage_a)
-    ws += stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, sa_batch).bytes;
+    ws += stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, sa_batch,
+                     d->trans_a ? 32 : 4).bytes;
   if (pl->stage_b)
-    ws += stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, sb_batch).bytes;
+    ws += stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, sb_batch,
+                     d->trans_b ? 4 : 32).bytes;
   if (pl->x3_split) {
-    ws += stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, sa_batch).bytes;
-    ws += stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, sb_batch).bytes;
+    ws += stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, sa_batch,
+                     d->trans_a ? 32 : 4).bytes;
+    ws += stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, sb_batch,
+                     d->trans_b ? 4 : 32).bytes;
   }
   if (pl->tri_diag) {
     ws += 2 * round_up(d->m * kTriDiagBlock * 4, 256);
@@ -642,8 +652,13 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   const int64_t a_batch = (d->stride_a == 0) ? 1 : d->batch;
   const int64_t b_batch = (d->stride_b == 0) ? 1 : d->batch;
   char* ws = static_cast<char*>(workspace);
+  // Extents of MN-major operands as the grouped loads see them (staged
+  // copies are zero-padded to 32 columns).
+  int64_t a_mn_ext = d->m, b_mn_ext = d->n;
   if (d->k > 0 && pl.stage_a) {
-    Stage g = stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, a_batch);
+    Stage g = stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, a_batch,
+                         d->trans_a ? 32 : 4);
+    if (d->trans_a) a_mn_ext = g.pitch;
     float* dst = reinterpret_cast<float*>(ws);
     const int64_t nrows = g.rows * g.nbatch;
     pitch_copy_kernel<<<static_cast<int>(std::min<int64_t>(nrows, 65535)), 256, 0, stream>>>(
@@ -654,7 +669,9 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     ws += g.bytes;
   }
   if (d->k > 0 && pl.stage_b) {
-    Stage g = stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, b_batch);
+    Stage g = stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, b_batch,
+                         d->trans_b ? 4 : 32);
+    if (!d->trans_b) b_mn_ext = g.pitch;
     float* dst = reinterpret_cast<float*>(ws);
     const int64_t nrows = g.rows * g.nbatch;
     pitch_copy_kernel<<<static_cast<int>(std::min<int64_t>(nrows, 65535)), 256, 0, stream>>>(
@@ -670,12 +687,14 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   const float* blo = nullptr;
   int64_t ldalo = 0, ldblo = 0, salo = 0, sblo = 0;
   if (pl.x3_split && d->k > 0) {
-    Stage ga = stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, a_batch);
+    Stage ga = stage_geom(d->trans_a ? d->k : d->m, d->trans_a ? d->m : d->k, a_batch,
+                          d->trans_a ? 32 : 4);
     float* da = reinterpret_cast<float*>(ws);
     ws += ga.bytes;
     split_lo_kernel<<<static_cast<int>(std::min<int64_t>(ga.rows * ga.nbatch, 65535)), 256, 0,
                       stream>>>(a, da, ga.rows, ga.cols, lda, sa, ga.pitch, ga.bstride, ga.nbatch);
-    Stage gb = stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, b_batch);
+    Stage gb = stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, b_batch,
+                          d->trans_b ? 4 : 32);
     float* db = reinterpret_cast<float*>(ws);
     ws += gb.bytes;
     split_lo_kernel<<<static_cast<int>(std::min<int64_t>(gb.rows * gb.nbatch, 65535)), 256, 0,
@@ -733,7 +752,10 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.splits = pl.splits;
   p.kb_total = static_cast<int>(cdiv(d->k, kBlockK));
   p.kb_per_split = pl.kb_per_split;
-  p.group_m = 8;
+  // Raster: groups of 8 tile-rows share B columns in L2; output-bound short-K
+  // problems instead walk along N so concurrent units write whole row runs
+  // (measured +3 % on 16384^2 x 32).
+  p.group_m = p.kb_total <= 8 ? 1 : 8;
   p.tri = d->op == B2G_OP_TRI_UPPER ? kTriUpper : (d->op == B2G_OP_TRI_LOWER ? kTriLower : kTriNone);
   p.a_batched = a_batch > 1;
   p.b_batched = b_batch > 1;
@@ -770,14 +792,14 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   if (!pl.a_mn_major) {
     ok = make_map(&ma, a, k_ext, d->m, a_batch, lda, sa, kBlockK, kBlockM, false);
   } else {
-    p.a_grouped = make_map_grouped(&ma, a, d->m, k_ext, a_batch, lda, sa, kBlockM / 32);
+    p.a_grouped = make_map_grouped(&ma, a, a_mn_ext, k_ext, a_batch, lda, sa, kBlockM / 32);
     ok = p.a_grouped || make_map(&ma, a, d->m, k_ext, a_batch, lda, sa, 32, kBlockK, true);
   }
   if (!ok) return B2G_ERR_UNSUPPORTED;
   if (!pl.b_mn_major) {
     ok = make_map(&mb, b, k_ext, d->n, b_batch, ldb, sb, kBlockK, bn_cta, false);
   } else {
-    p.b_grouped = make_map_grouped(&mb, b, d->n, k_ext, b_batch, ldb, sb, bn_cta / 32);
+    p.b_grouped = make_map_grouped(&mb, b, b_mn_ext, k_ext, b_batch, ldb, sb, bn_cta / 32);
     ok = p.b_grouped || make_map(&mb, b, d->n, k_ext, b_batch, ldb, sb, 32, kBlockK, true);
   }
   if (!ok) return B2G_ERR_UNSUPPORTED;
@@ -795,14 +817,14 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     if (!pl.a_mn_major)
       ok = make_map(&mad, alo, k_ext, d->m, a_batch, ldalo, salo, kBlockK, kBlockM, false);
     else if (p.a_grouped)
-      ok = make_map_grouped(&mad, alo, d->m, k_ext, a_batch, ldalo, salo, kBlockM / 32);
+      ok = make_map_grouped(&mad, alo, a_mn_ext, k_ext, a_batch, ldalo, salo, kBlockM / 32);
     else
       ok = make_map(&mad, alo, d->m, k_ext, a_batch, ldalo, salo, 32, kBlockK, true);
     if (!ok) return B2G_ERR_UNSUPPORTED;
     if (!pl.b_mn_major)
       ok = make_map(&mbd, blo, k_ext, d->n, b_batch, ldblo, sblo, kBlockK, bn_cta, false);
     else if (p.b_grouped)
-      ok = make_map_grouped(&mbd, blo, d->n, k_ext, b_batch, ldblo, sblo, bn_cta / 32);
+      ok = make_map_grouped(&mbd, blo, b_mn_ext, k_ext, b_batch, ldblo, sblo, bn_cta / 32);
     else
       ok = make_map(&mbd, blo, d->n, k_ext, b_batch, ldblo, sblo, 32, kBlockK, true);
     if (!ok) return B2G_ERR_UNSUPPORTED;
@@ -835,8 +857,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     if (pl.block_n == 512)
       return launch_majors<512, 4, false, false, true>(a_mn, b_mn, maps, p, grid, stream);
     if (pl.block_n == 256)
-      return launch_majors<256, B2G_PAIR256_STAGES, false, false, true, B2G_PAIR256_EPIG>(
-          a_mn, b_mn, maps, p, grid, stream);
+      return launch_majors<256, B2G_PAIR256_STAGES, false, false, true, B2G_PAIR256_EPIG,
+                           B2G_PAIR256_EPIW>(a_mn, b_mn, maps, p, grid, stream);
     return launch_majors<128, 8, false, false, true>(a_mn, b_mn, maps, p, grid, stream);
   }
   if (pl.block_n == 256)

@@ -183,7 +183,8 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
 // per operand byte streamed from L2, at the price of a single-buffered
 // accumulator (512 TMEM columns), so its epilogue does not overlap the next
 // unit's mainloop.
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG = 1>
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG = 1,
+          int EPIW = 8>
 struct EngineCfg {
   static constexpr int kCtas = PAIR ? 2 : 1;
   static constexpr int kUnitM = kBlockM * kCtas;
@@ -202,7 +203,9 @@ struct EngineCfg {
   static constexpr int kOffALo = STAGES * (kABytes + kBBytes);
   static constexpr int kOffBLo = kOffALo + STAGES * kABytes;
   static constexpr int kOffEpi = STAGES * (kABytes + kBBytes) * kOperandBufs;
-  static constexpr int kEpiWarps = 8;                        // two per TMEM lane quadrant
+  static constexpr int kEpiWarps = EPIW;                     // EPIW / 4 per TMEM lane quadrant
+  static constexpr int kEpiParts = EPIW / 4;
+  static_assert(EPIW % 4 == 0 && EPIW >= 4, "epilogue warps come in quadrant sets");
   static constexpr int kEpiBufBytes = 32 * 32 * 4;           // one 32 x 32 fp32 box
   static constexpr int kEpiBufs = EPIG;                      // staging boxes per epilogue warp
   static constexpr int kEpiGroup = EPIG;                     // chunks staged per fence
@@ -469,14 +472,16 @@ __device__ __forceinline__ void store_group_tma(const EngineParams& p, const CUt
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG>
-__global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>::kThreads, 1)
+template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG,
+          int EPIW>
+__global__ void __launch_bounds__(
+    EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG, EPIW>::kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap map_a,
                      const __grid_constant__ CUtensorMap map_b,
                      const __grid_constant__ CUtensorMap map_c,
                      const __grid_constant__ CUtensorMap map_ad,
                      const __grid_constant__ CUtensorMap map_bd, const EngineParams p) {
-  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG>;
+  using Cfg = EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR, EPIG, EPIW>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -778,11 +783,12 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
     }
   } else if (warp < 2 + Cfg::kEpiWarps) {
     // ------------------------------------------------------------ epilogue
-    // Warp e (0..7) reads TMEM lane quadrant warp % 4 (the hardware rule)
-    // and every other 32-column chunk starting at e / 4.
+    // Epilogue warp e reads TMEM lane quadrant warp % 4 (the hardware rule)
+    // and every kEpiParts-th 32-column chunk starting at e / 4.
+    constexpr int kParts = Cfg::kEpiParts;
     const int quad = warp & 3;
     const int ew = warp - 2;
-    const int half = ew >> 2;
+    const int half = ew >> 2;   // this warp's part: chunks half, half + kParts, ...
     float* stg = reinterpret_cast<float*>(smem + Cfg::kOffEpi) + ew * Cfg::kEpiBufs * 32 * 32;
     const uint32_t tmem_empty_leader =
         PAIR ? ptx::mapa_shared(ptx::smem_addr(tmem_empty), 0) : 0u;
@@ -804,7 +810,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            for (int ch = half; ch * 32 < BN && n0 + ch * 32 < p.N; ch += 2)
+            for (int ch = half; ch * 32 < BN && n0 + ch * 32 < p.N; ch += kParts)
               ptx::tma_store_3d(&map_c, stg, n0 + ch * 32, row0, u.b);
             ptx::bulk_commit();
           }
@@ -815,9 +821,11 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
         // Structurally zero tile (or K == 0): write zeros unless accumulating.
         if (!p.atomic_out && !u.accumulate && row0 < p.M) {
           float* cb = p.C + static_cast<long long>(u.b) * p.stride_c;
-          for (int it = 0; it < 8 * (BN / 64); ++it) {
+          for (int it = 0; it < 8 * (BN / 32); ++it) {
+            const int cc = it >> 3;                      // 32-column chunk
+            if (cc % kParts != half) continue;
             const int r_local = (it & 7) * 4 + (lane >> 3);
-            const int gcol = n0 + ((it >> 3) * 2 + half) * 32 + (lane & 7) * 4;
+            const int gcol = n0 + cc * 32 + (lane & 7) * 4;
             const int grow = row0 + r_local;
             if (grow < p.M && gcol < p.N)
               store4(p, cb + static_cast<long long>(grow) * p.ldc, grow, gcol, 0.f, 0.f, 0.f, 0.f);
@@ -848,7 +856,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
         // TMA path: groups of kEpiGroup chunks, one TMEM wait and one fence each.
         constexpr int G = Cfg::kEpiGroup;
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
-        const int mine = (nch - half + 1) / 2;                 // chunks half, half+2, ...
+        const int mine = (nch - half + kParts - 1) / kParts;   // chunks half, half+kParts, ...
 #pragma unroll 1
         for (int g0 = 0; g0 < mine; g0 += G) {
           const int ng = mine - g0 < G ? mine - g0 : G;
@@ -856,7 +864,7 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
           int col0[G];
 #pragma unroll
           for (int g = 0; g < G; ++g) {
-            const int ch = half + 2 * (g0 + (g < ng ? g : 0));
+            const int ch = half + kParts * (g0 + (g < ng ? g : 0));
             col0[g] = n0 + ch * 32;
             if (g < ng) ptx::tmem_ld_32x32b_x32(taddr + ch * 32, r[g]);
           }
@@ -874,10 +882,10 @@ __global__ void __launch_bounds__(EngineCfg<BN, STAGES, A_MN, B_MN, X3, XF, PAIR
         ptx::tmem_ld_32x32b_x32(taddr + half * 32, ra);
         tmem_ld_wait_regs(ra);
 #pragma unroll 1
-        for (int ch = half; ch < nch; ch += 2) {
-          const bool more = ch + 2 < nch;
+        for (int ch = half; ch < nch; ch += kParts) {
+          const bool more = ch + kParts < nch;
           if (more)
-            ptx::tmem_ld_32x32b_x32(taddr + (ch + 2) * 32, rb);   // in flight while ra drains
+            ptx::tmem_ld_32x32b_x32(taddr + (ch + kParts) * 32, rb);   // in flight while ra drains
           else
             release();                                            // every TMEM read is done
 #ifndef B2G_EXP_NO_STORES

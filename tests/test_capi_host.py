@@ -111,7 +111,7 @@ def test_plan_irregular_stages_unaligned_operands(capi):
     p = _plan(capi, 8205, 5921, 2949)
     assert p.stage_a == 1 and p.stage_b == 1
     pitch_a = (2949 + 3) // 4 * 4
-    pitch_b = (5921 + 3) // 4 * 4
+    pitch_b = (5921 + 31) // 32 * 32     # MN-major B: zero-padded to 32 columns
     exp = ((8205 * pitch_a * 4 + 255) // 256 + (2949 * pitch_b * 4 + 255) // 256) * 256
     assert p.workspace_bytes == exp
     assert capi.lib().b2g_gemm_workspace_bytes(
