@@ -366,20 +366,6 @@ __device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtenso
     for (int j = 0; j < 32; ++j)
       if (col0 + j > row) r[j] = 0u;
   }
-#ifdef B2G_EXP_DIRECT_ROWS
-  if (p.tma_store) {
-    if (row < p.M) {
-      float* crow = p.C + static_cast<long long>(b) * p.stride_c + static_cast<long long>(row) * p.ldc;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (col0 + 4 * j + 3 < p.N)
-          *reinterpret_cast<float4*>(crow + col0 + 4 * j) =
-              make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-    }
-    return;
-  }
-#endif
   if (p.tma_store) {
     // NBUF staging boxes per warp: wait until the store issued from this
     // box NBUF chunks ago has read it (up to NBUF - 1 stay in flight).
@@ -562,10 +548,6 @@ __global__ void __launch_bounds__(
             ok = false;
             break;
           }
-#ifdef B2G_EXP_NO_LOADS
-          if (!PAIR || leader) ptx::mbar_arrive(&full[s]);
-          continue;
-#endif
           // Each CTA's loads complete on its own barrier when transform warps
           // must see them; otherwise a pair's loads complete on the leader's.
           if (!PAIR || XF)
@@ -888,9 +870,7 @@ __global__ void __launch_bounds__(
             ptx::tmem_ld_32x32b_x32(taddr + (ch + kParts) * 32, rb);   // in flight while ra drains
           else
             release();                                            // every TMEM read is done
-#ifndef B2G_EXP_NO_STORES
           store_chunk<Cfg::kEpiBufs>(p, &map_c, stg, seq, ra, u.b, row0, n0 + ch * 32, lane);
-#endif
           if (more) {
             tmem_ld_wait_regs(rb);
 #pragma unroll
