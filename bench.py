@@ -222,11 +222,16 @@ def device_inputs(w, seed_offset=0, **shapes):
     if n == "symmetric":
         X, Y = r(s["n"], s["n"]), r(s["n"], s["n"])
         return (X + X.T) / 2, (Y + Y.T) / 2
+    if n == "pointwise_conv":
+        return (r(s["batch"], s["cin"], s["h"], s["w"]), r(s["cout"], s["cin"], 1, 1),
+                r(s["cout"]))
     raise KeyError(n)
 
 
-def cublas_fn(name, A, B):
+def cublas_fn(name, A, B, *rest):
     """The same math through torch (cuBLAS TF32) for the comparison column."""
+    if name == "pointwise_conv":   # cuDNN conv2d (TF32 allowed by default)
+        return lambda: torch.nn.functional.conv2d(A, B, rest[0])
     if name == "transposed_a":
         return lambda: torch.matmul(A.t(), B)
     if name == "transposed_b":
@@ -267,10 +272,11 @@ REF_SAFE = {  # workload -> reference PID whose kernel runs on the workload
     "square": 1, "batched": 3, "large_k": 6, "small_k": 7, "irregular": 8, "tall_skinny": 9,
     "tensor3d": 10, "tensor4d": 11, "diag": 12, "symmetric": 13, "upper_tri": 14,
     "lower_tri": 15, "transposed_a": 16, "transposed_b": 17, "transposed_both": 18,
+    "pointwise_conv": 87,
 }
 
 
-def reference_callable(name, A, B):
+def reference_callable(name, A, B, *rest):
     from oracle import build_ref
 
     if name == "gemv":
@@ -287,6 +293,8 @@ def reference_callable(name, A, B):
         return (lambda: f(Ap, Bp)), "zero-padded to K=64 (K7's own contract)"
     if name == "tall_skinny":
         return (lambda: f(A, B)), "as is; K9 uses only 32 of the 64 inner columns (parity FAIL)"
+    if name == "pointwise_conv":
+        return (lambda: f(A, B, rest[0])), "float32 dispatch only (its double instance fails ptxas)"
     return (lambda: f(A, B)), None
 
 
@@ -504,10 +512,10 @@ def shape_table(W, peaks, only, ops):
     for name, w in W.items():
         if name == HEADLINE or (only and name not in only):
             continue
-        A, B = device_inputs(w)
+        args = device_inputs(w)
         op = ops.OPERATORS[w.pid].forward
         row = {"pid": w.pid, "shapes": w.shapes}
-        ours = lambda: op(A, B)
+        ours = lambda: op(*args)
         k = adaptive_steps(ours)
         _, ms = time_loop(ours, k, 3)
         row["ours"] = roofline(w, ms, peaks)
@@ -519,12 +527,12 @@ def shape_table(W, peaks, only, ops):
                 _, ms3 = time_loop(ours, k, 3)
             row["ours_3xtf32"] = {"ms": round(ms3, 4),
                                   "tflops": round(w.flops / (ms3 / 1e3) / 1e12, 2)}
-        cb = cublas_fn(name, A, B)
+        cb = cublas_fn(name, *args)
         _, msb = time_loop(cb, k, 3)
         fl = w.useful_flops or w.flops
         row["cublas_tf32"] = {"ms": round(msb, 4), "tflops": round(fl / (msb / 1e3) / 1e12, 2)}
         try:
-            rf, note = reference_callable(name, A, B)
+            rf, note = reference_callable(name, *args)
             kr = adaptive_steps(rf, target_s=0.2, hi=200)
             _, msr = time_loop(rf, kr, 3)
             row["reference"] = {"ms": round(msr, 4),
@@ -535,7 +543,7 @@ def shape_table(W, peaks, only, ops):
         except Exception as e:
             row["reference"] = {"unavailable": str(e)[:120]}
         out[name] = row
-        del A, B
+        del args
         torch.cuda.empty_cache()
     return out
 

@@ -74,6 +74,14 @@ def lib(path: Path | None = None) -> C.CDLL:
         h.b2g_gemv.restype = C.c_int
         h.b2g_scale.argtypes = [C.c_void_p, C.c_float, C.c_void_p, C.c_int64, C.c_void_p]
         h.b2g_scale.restype = C.c_int
+        h.b2g_pointwise_conv_workspace_bytes.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p,
+                                                         C.c_int64, C.c_int64, C.c_int64,
+                                                         C.c_int64, C.c_int]
+        h.b2g_pointwise_conv_workspace_bytes.restype = C.c_int64
+        h.b2g_pointwise_conv.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int,
+                                         C.c_void_p, C.c_int64, C.c_void_p]
+        h.b2g_pointwise_conv.restype = C.c_int
         h.b2g_read_device_error.argtypes = [C.c_int, C.POINTER(C.c_int32)]
         h.b2g_read_device_error.restype = C.c_int
         h.b2g_status_string.argtypes = [C.c_int]
@@ -118,6 +126,19 @@ def gemm_noalloc(desc: GemmDesc, stream: int = 0) -> int:
 
 def rowscale(d, b, out, rows, cols, ldb, ldo, stream: int = 0) -> int:
     return lib().b2g_rowscale(d, b, out, rows, cols, ldb, ldo, C.c_void_p(stream))
+
+
+def pointwise_conv_workspace_bytes(inp, weight, out, batch, cin, cout, spatial,
+                                   precision=PREC_TF32) -> int:
+    return lib().b2g_pointwise_conv_workspace_bytes(inp, weight, out, batch, cin, cout, spatial,
+                                                    precision)
+
+
+def pointwise_conv(inp, weight, bias, out, batch, cin, cout, spatial, precision=PREC_TF32,
+                   workspace=0, workspace_bytes=0, stream: int = 0) -> int:
+    """out[n] = weight . in[n] (+ bias per output channel), NCHW with H*W = spatial."""
+    return lib().b2g_pointwise_conv(inp, weight, bias, out, batch, cin, cout, spatial, precision,
+                                    workspace, workspace_bytes, C.c_void_p(stream))
 
 
 def read_device_error(device: int = 0) -> int:

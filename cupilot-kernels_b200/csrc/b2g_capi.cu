@@ -645,7 +645,7 @@ extern "C" int64_t b2g_gemm_workspace_bytes(const b2g_gemm_desc* d) {
 // checked: staged copies of unaligned operands, tensor maps, split-K clear
 // of C, and the engine launch.
 static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* workspace,
-                       int* err_word, cudaStream_t stream) {
+                       int* err_word, cudaStream_t stream, const float* row_bias = nullptr) {
   const float* a = d->a;
   const float* b = d->b;
   int64_t lda = d->lda, ldb = d->ldb, sa = d->stride_a, sb = d->stride_b;
@@ -773,6 +773,7 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.tri_diag = pl.tri_diag;
   p.unit_table = table;
   p.diag_oob_row = static_cast<int>(d->m);
+  p.row_bias = row_bias;
   p.err = err_word;
 
   if (p.atomic_out) {
@@ -879,6 +880,85 @@ extern "C" int b2g_gemm(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {
   if (pl.workspace_bytes > 0 && (!d->workspace || d->workspace_bytes < pl.workspace_bytes))
     return B2G_ERR_WORKSPACE;
   return run_planned(d, pl, d->workspace, ds->err_word, stream);
+}
+
+namespace b2g {
+namespace {
+// in_channels == 0: every output of channel o is bias[o] (or 0).
+__global__ void conv_bias_fill_kernel(const float* __restrict__ bias, float* __restrict__ out,
+                                      int64_t planes, int64_t cout, int64_t spatial) {
+  for (int64_t pl = blockIdx.x; pl < planes; pl += gridDim.x) {
+    const float v = bias ? bias[pl % cout] : 0.f;
+    float* o = out + pl * spatial;
+    for (int64_t i = threadIdx.x; i < spatial; i += blockDim.x) o[i] = v;
+  }
+}
+
+// The batched GEMM a pointwise convolution runs as: out[n] = W . in[n].
+bool conv_desc(int64_t batch, int64_t cin, int64_t cout, int64_t spatial, int precision,
+               b2g_gemm_desc* d) {
+  if (batch < 0 || cin < 0 || cout < 0 || spatial < 0) return false;
+  std::memset(d, 0, sizeof(*d));
+  d->op = B2G_OP_GEMM;
+  d->precision = precision;
+  d->m = cout;
+  d->n = spatial;
+  d->k = cin;
+  d->batch = std::max<int64_t>(batch, 1);
+  d->lda = std::max<int64_t>(cin, 1);
+  d->stride_a = 0;   // one weight for every image
+  d->ldb = std::max<int64_t>(spatial, 1);
+  d->stride_b = cin * spatial;
+  d->ldc = std::max<int64_t>(spatial, 1);
+  d->stride_c = cout * spatial;
+  return true;
+}
+}  // namespace
+}  // namespace b2g
+
+extern "C" int64_t b2g_pointwise_conv_workspace_bytes(const float* in, const float* weight,
+                                                      const float* out, int64_t batch,
+                                                      int64_t cin, int64_t cout, int64_t spatial,
+                                                      int precision) {
+  b2g_gemm_desc d;
+  if (!conv_desc(batch, cin, cout, spatial, precision, &d)) return -1;
+  if (batch == 0 || cout == 0 || spatial == 0) return 0;
+  d.a = weight;
+  d.b = in;
+  d.c = const_cast<float*>(out);
+  return b2g_gemm_workspace_bytes(&d);
+}
+
+extern "C" int b2g_pointwise_conv(const float* in, const float* weight, const float* bias,
+                                  float* out, int64_t batch, int64_t cin, int64_t cout,
+                                  int64_t spatial, int precision, void* workspace,
+                                  int64_t workspace_bytes, b2g_stream_t stream_handle) {
+  b2g_gemm_desc d;
+  if (!conv_desc(batch, cin, cout, spatial, precision, &d)) return B2G_ERR_INVALID_ARG;
+  if (batch == 0 || cout == 0 || spatial == 0) return B2G_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  if (!out) return B2G_ERR_INVALID_ARG;
+  if (cin == 0) {
+    const int64_t planes = batch * cout;
+    conv_bias_fill_kernel<<<static_cast<unsigned>(std::min<int64_t>(planes, 65535)), 256, 0,
+                            stream>>>(bias, out, planes, cout, spatial);
+    return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
+  }
+  d.a = weight;
+  d.b = in;
+  d.c = out;
+  d.workspace = workspace;
+  d.workspace_bytes = workspace_bytes;
+  if (!valid_desc(&d)) return B2G_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  int rc = device_state(&ds);
+  if (rc != B2G_OK) return rc;
+  b2g_gemm_plan pl;
+  rc = b2g_gemm_plan_for(&d, ds->num_sms, &pl);
+  if (rc != B2G_OK) return rc;
+  if (pl.workspace_bytes > 0 && (!workspace || workspace_bytes < pl.workspace_bytes))
+    return B2G_ERR_WORKSPACE;
+  return run_planned(&d, pl, workspace, ds->err_word, stream, bias);
 }
 
 extern "C" int b2g_rowscale(const float* d, const float* b, float* out, int64_t rows, int64_t cols,

@@ -66,6 +66,7 @@ struct EngineParams {
   int tri_diag;                // triangular inputs masked through diagonal-block copies
   const int4* unit_table;      // if set: unit w is {tm, tn, kb_lo, kb_hi | flags << 24}
   int diag_oob_row;            // a K row past every operand row (zero-filled by TMA)
+  const float* row_bias;       // if set: C[b][i][j] += row_bias[i] (added by the K piece at 0)
   int* err;
 };
 
@@ -786,9 +787,10 @@ __global__ void __launch_bounds__(
         if (!p.atomic_out && !u.accumulate && row0 < p.M) {
           if (lane == 0) ptx::bulk_wait_read<0>();
           __syncwarp();
+          const float z = (p.row_bias && row0 + lane < p.M) ? p.row_bias[row0 + lane] : 0.f;
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<float4*>(stg + lane * 32 + j * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(stg + lane * 32 + j * 4) = make_float4(z, z, z, z);
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
@@ -809,8 +811,10 @@ __global__ void __launch_bounds__(
             const int r_local = (it & 7) * 4 + (lane >> 3);
             const int gcol = n0 + cc * 32 + (lane & 7) * 4;
             const int grow = row0 + r_local;
-            if (grow < p.M && gcol < p.N)
-              store4(p, cb + static_cast<long long>(grow) * p.ldc, grow, gcol, 0.f, 0.f, 0.f, 0.f);
+            if (grow < p.M && gcol < p.N) {
+              const float z = p.row_bias ? p.row_bias[grow] : 0.f;
+              store4(p, cb + static_cast<long long>(grow) * p.ldc, grow, gcol, z, z, z, z);
+            }
           }
         }
         continue;
@@ -834,6 +838,9 @@ __global__ void __launch_bounds__(
       };
       int nch = (p.N - n0 + 31) / 32;
       if (nch > BN / 32) nch = BN / 32;
+      // Row bias (this lane's output row), added once: by the K piece that starts at 0.
+      const bool with_bias = p.row_bias != nullptr && u.kb_lo == 0;
+      const float bias_v = (with_bias && row0 + lane < p.M) ? p.row_bias[row0 + lane] : 0.f;
       if (row0 < p.M && half < nch && p.tma_store) {
         // TMA path: groups of kEpiGroup chunks, one TMEM wait and one fence each.
         constexpr int G = Cfg::kEpiGroup;
@@ -855,6 +862,12 @@ __global__ void __launch_bounds__(
           for (int g = 0; g < G; ++g)
 #pragma unroll
             for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[g][i]));
+          if (with_bias) {
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+              for (int i = 0; i < 32; ++i) r[g][i] = __float_as_uint(__uint_as_float(r[g][i]) + bias_v);
+          }
           if (g0 + G >= mine) release();                      // every TMEM read is done
           store_group_tma<G>(p, &map_c, stg, r, ng, u.b, row0, col0, lane, u.accumulate);
         }
@@ -870,6 +883,10 @@ __global__ void __launch_bounds__(
             ptx::tmem_ld_32x32b_x32(taddr + (ch + kParts) * 32, rb);   // in flight while ra drains
           else
             release();                                            // every TMEM read is done
+          if (with_bias) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ra[i] = __float_as_uint(__uint_as_float(ra[i]) + bias_v);
+          }
           store_chunk<Cfg::kEpiBufs>(p, &map_c, stg, seq, ra, u.b, row0, n0 + ch * 32, lane);
           if (more) {
             tmem_ld_wait_regs(rb);

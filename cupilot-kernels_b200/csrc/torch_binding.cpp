@@ -285,6 +285,50 @@ at::Tensor matrix_scalar_mult(at::Tensor A, double s) {
   return C;
 }
 
+// kernels/87_conv_pointwise_2D_best_kernel.cu:451 (pointwise_conv_cuda) —
+// out (N, Cout, H, W) = 1x1 convolution of input (N, Cin, H, W) with weight
+// (Cout, Cin) or (Cout, Cin, 1, 1), plus an optional per-channel bias.
+at::Tensor pointwise_conv(at::Tensor input, at::Tensor weight, c10::optional<at::Tensor> bias_opt) {
+  check_input(input, "input");
+  check_input(weight, "weight");
+  TORCH_CHECK(input.dim() == 4, "input must be (batch, in_channels, height, width)");
+  TORCH_CHECK(weight.dim() == 2 || (weight.dim() == 4 && weight.size(2) == 1 && weight.size(3) == 1),
+              "weight must be (out_channels, in_channels) or (out_channels, in_channels, 1, 1)");
+  const int64_t bs = input.size(0), cin = input.size(1), h = input.size(2), w = input.size(3);
+  const int64_t cout = weight.size(0);
+  TORCH_CHECK(weight.size(1) == cin, "weight has ", weight.size(1), " input channels, input has ",
+              cin);
+  TORCH_CHECK(input.device() == weight.device(), "input and weight must be on the same device");
+  at::Tensor bias;
+  if (bias_opt.has_value() && bias_opt->defined()) {
+    bias = *bias_opt;
+    check_input(bias, "bias");
+    TORCH_CHECK(bias.numel() == cout, "bias must have out_channels elements");
+    TORCH_CHECK(bias.device() == input.device(), "bias must be on the input's device");
+    bias = bias.contiguous();
+  }
+  const c10::cuda::CUDAGuard guard(input.device());
+  at::Tensor out = at::empty({bs, cout, h, w}, input.options());
+  if (out.numel() == 0) return out;
+  TORCH_CHECK(bs <= 65535, "batch too large");
+  at::Tensor x = input.contiguous();
+  at::Tensor wt = weight.contiguous();
+  const float* bp = bias.defined() ? bias.data_ptr<float>() : nullptr;
+  const int prec = g_precision.load();
+  const int64_t ws = b2g_pointwise_conv_workspace_bytes(x.data_ptr<float>(), wt.data_ptr<float>(),
+                                                        out.data_ptr<float>(), bs, cin, cout,
+                                                        h * w, prec);
+  TORCH_CHECK(ws >= 0, "b2g: invalid pointwise convolution");
+  at::Tensor wst;
+  if (ws > 0) wst = at::empty({ws}, input.options().dtype(at::kByte));
+  auto stream = at::cuda::getCurrentCUDAStream(input.device().index());
+  check_status(b2g_pointwise_conv(x.data_ptr<float>(), wt.data_ptr<float>(), bp,
+                                  out.data_ptr<float>(), bs, cin, cout, h * w, prec,
+                                  ws > 0 ? wst.data_ptr() : nullptr, ws, stream.stream()),
+               "b2g_pointwise_conv");
+  return out;
+}
+
 // Generic entry: op(A) . op(B) with explicit flags (used by the partitioner).
 at::Tensor gemm(at::Tensor A, at::Tensor B, bool trans_a, bool trans_b, int64_t op) {
   return matmul_2d(trans_a ? A.t() : A, trans_b ? B.t() : B, static_cast<int>(op));
@@ -325,6 +369,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("matmul_transposed_both", &matmul_transposed_both);
   m.def("gemv", &gemv);
   m.def("matrix_scalar_mult", &matrix_scalar_mult);
+  m.def("pointwise_conv", &pointwise_conv, "1x1 convolution, NCHW", py::arg("input"),
+        py::arg("weight"), py::arg("bias") = py::none());
   m.def("gemm", &gemm, "op(A) . op(B)", py::arg("A"), py::arg("B"), py::arg("trans_a") = false,
         py::arg("trans_b") = false, py::arg("op") = 0);
   m.def("set_precision", &set_precision);

@@ -64,8 +64,8 @@ class Operator:
     ref_site: str           # reference file:line of that function
     forward: Callable
 
-    def __call__(self, A, B):
-        return self.forward(A, B)
+    def __call__(self, *args, **kwargs):
+        return self.forward(*args, **kwargs)
 
     def __getattr__(self, item):
         if item == self.ref_name:
@@ -120,6 +120,9 @@ OPERATORS = {
     18: Operator(18, "transposed_both", "matmul_transposed_cuda",
                  _K + "18_Matmul_with_transposed_both_best_kernel.cu:152",
                  _ext.matmul_transposed_both),
+    # forward(input, weight, bias=None): NCHW 1x1 convolution as a batched GEMM
+    87: Operator(87, "pointwise_conv", "pointwise_conv_cuda",
+                 _K + "87_conv_pointwise_2D_best_kernel.cu:451", _ext.pointwise_conv),
 }
 
 for _pid, _op in OPERATORS.items():

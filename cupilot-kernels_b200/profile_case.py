@@ -34,10 +34,10 @@ def main():
     w = W[args.workload]
     over = {k: int(v) for k, v in (x.split("=") for x in args.set)}
     ops.set_precision(args.precision)
-    A, B = bench.device_inputs(w, **over)
+    call_args = bench.device_inputs(w, **over)
     op = ops.OPERATORS[w.pid].forward
     for _ in range(args.iters):
-        op(A, B)
+        op(*call_args)
         torch.cuda.synchronize()
     print(f"{args.workload} {dict(w.shapes, **over)} x{args.iters} ok")
 

@@ -32,13 +32,15 @@ class Workload:
     useful_flops: float = 0.0  # triangular ops: flops of the non-zero band
 
     def inputs(self, device="cpu", **override):
+        """The operator's arguments (A, B — or input, weight, bias for the
+        pointwise convolution), seeded on the CPU."""
         shapes = dict(self.shapes)
         shapes.update(override)
         g = torch.Generator().manual_seed(self.seed)
-        A, B = self.make(g, **shapes)
+        args = self.make(g, **shapes)
         if device != "cpu":
-            A, B = A.to(device), B.to(device)
-        return A, B
+            args = tuple(t.to(device) if isinstance(t, torch.Tensor) else t for t in args)
+        return args
 
 
 def _randn(g, *shape):
@@ -97,6 +99,16 @@ def _mk_gemv(g, m, k):
 
 def _mk_scalar(g, m, n):
     return _randn(g, m, n), 2.5
+
+
+def _mk_conv(g, batch, cin, cout, h, w):
+    return _randn(g, batch, cin, h, w), _randn(g, cout, cin, 1, 1), _randn(g, cout)
+
+
+def _conv_cost(batch, cin, cout, h, w):
+    s = h * w
+    flops = 2.0 * batch * cout * cin * s
+    return flops, 4.0 * (batch * cin * s + cout * cin + cout + batch * cout * s)
 
 
 def _gemm_cost(m, n, k, batch=1, a_shared=False, b_shared=False):
@@ -159,6 +171,14 @@ _add(Workload("matrix_scalar", 5, dict(m=16384, n=16384), 16, _mk_scalar, 16384.
               4.0 * 2 * 16384 * 16384, "hbm"))
 
 
+# Next row (reference PID 87): the pointwise convolution.  No benchmark
+# config names its size; out_channels = 128 is the size its kernel is tuned
+# for (kernels/87_conv_pointwise_2D_best_kernel.cu:183), the rest is chosen:
+# 16 images of 64 x 256 x 256, 0.27 GB in and 0.54 GB out (HBM-bound).
+_add(_w("pointwise_conv", 87, dict(batch=16, cin=64, cout=128, h=256, w=256), 17, _mk_conv,
+        _conv_cost(16, 64, 128, 256, 256), "hbm"))
+
+
 def cost_for(name: str, **shapes) -> Tuple[float, float]:
     """(flops, min_bytes) of a workload at overridden shapes."""
     w = WORKLOADS[name]
@@ -180,5 +200,7 @@ def cost_for(name: str, **shapes) -> Tuple[float, float]:
         return 2.0 * s["m"] * s["k"], 4.0 * (s["m"] * s["k"] + s["m"] + s["k"])
     if name == "matrix_scalar":
         return float(s["m"] * s["n"]), 8.0 * s["m"] * s["n"]
+    if name == "pointwise_conv":
+        return _conv_cost(s["batch"], s["cin"], s["cout"], s["h"], s["w"])
     n = s["n"]
     return _gemm_cost(n, n, n)

@@ -30,6 +30,7 @@
  *   kernels/18_Matmul_with_transposed_both_best_kernel.cu:152   matmul_transposed_cuda   -> b2g_gemm (TT)
  *   kernels/4_Matrix_vector_multiplication_best_kernel.cu:84    gemv_cuda                -> b2g_gemv
  *   kernels/5_Matrix_scalar_multiplication_best_kernel.cu:47    matrix_scalar_mult_cuda  -> b2g_scale
+ *   kernels/87_conv_pointwise_2D_best_kernel.cu:451             pointwise_conv_cuda      -> b2g_pointwise_conv
  *
  * Error behaviour: every entry point returns a b2g_status; 0 is success.
  * Nothing traps or asserts on the device.  Kernel-side waits are bounded;
@@ -173,6 +174,28 @@ B2G_API int b2g_gemv(const float* a, int64_t lda, const float* x, float* y, int6
  * Replaces matrix_scalar_mult_cuda (kernels/5_Matrix_scalar_multiplication_best_kernel.cu:47).
  */
 B2G_API int b2g_scale(const float* a, float s, float* out, int64_t n, b2g_stream_t stream);
+
+/*
+ * Pointwise (1x1, stride 1, no padding) convolution over NCHW fp32 tensors:
+ *   out[n][o][s] = sum_c weight[o][c] * in[n][c][s] + (bias ? bias[o] : 0)
+ * with s = h * W + w running over the `spatial` = H * W positions.  Each
+ * image is one GEMM of the shared weight (out_channels x in_channels) by the
+ * image (in_channels x spatial); the batch runs as one batched launch and
+ * the bias is added in the epilogue.  `precision` as in b2g_gemm_desc.
+ * Inputs are dense (in: batch x in_channels x spatial, weight: out_channels
+ * x in_channels, out: batch x out_channels x spatial).  in_channels == 0
+ * writes the bias (or zeros).  The workspace size depends on the pointers'
+ * alignment (unaligned operands are staged), so it takes the same pointers.
+ * Replaces pointwise_conv_cuda (kernels/87_conv_pointwise_2D_best_kernel.cu:451).
+ */
+B2G_API int64_t b2g_pointwise_conv_workspace_bytes(const float* in, const float* weight,
+                                                   const float* out, int64_t batch,
+                                                   int64_t in_channels, int64_t out_channels,
+                                                   int64_t spatial, int precision);
+B2G_API int b2g_pointwise_conv(const float* in, const float* weight, const float* bias,
+                               float* out, int64_t batch, int64_t in_channels,
+                               int64_t out_channels, int64_t spatial, int precision,
+                               void* workspace, int64_t workspace_bytes, b2g_stream_t stream);
 
 /* Read and clear the device-side error word of `device` (synchronises it). */
 B2G_API int b2g_read_device_error(int device, int32_t* code);

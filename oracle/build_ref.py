@@ -48,6 +48,7 @@ REF_FUNCS = {
     16: ("16_Matmul_with_transposed_A_best_kernel.cu", "matmul_transposed_cuda", 124),
     17: ("17_Matmul_with_transposed_B_best_kernel.cu", "matmul_cuda", 267),
     18: ("18_Matmul_with_transposed_both_best_kernel.cu", "matmul_transposed_cuda", 152),
+    87: ("87_conv_pointwise_2D_best_kernel.cu", "pointwise_conv_cuda", 451),
 }
 
 EXT = sysconfig.get_config_var("EXT_SUFFIX")
@@ -83,16 +84,33 @@ def build_one(pid: int, verbose: bool = False, force: bool = False) -> Path:
     obj = OUT / f"ref_p{pid}.o"
     shim = OUT / f"ref_p{pid}_shim.cpp"
     second = "float s" if pid == 5 else "torch::Tensor B"   # K5 takes a scalar (K5:47)
+    if pid == 87:   # K87:451 takes (input, weight, optional bias)
+        second = "torch::Tensor B, c10::optional<torch::Tensor> bias"
+    extra = ', py::arg("input"), py::arg("weight"), py::arg("bias") = py::none()' if pid == 87 else ""
     shim.write_text(
         "#include <torch/extension.h>\n"
         f"torch::Tensor {func}(torch::Tensor A, {second});\n"
-        f"PYBIND11_MODULE({name}, m) {{ m.def(\"{func}\", &{func}); }}\n")
+        f"PYBIND11_MODULE({name}, m) {{ m.def(\"{func}\", &{func}{extra}); }}\n")
+    pre = []
+    if pid == 87:
+        # As shipped, K87's AT_DISPATCH_FLOATING_TYPES_AND2 also instantiates
+        # its kernel for double, which needs 0xc500 bytes of static shared
+        # memory (> 0xc000) and fails ptxas.  A force-included header
+        # narrows that dispatch to float32 (the type every test and the
+        # bench use); the kernel source itself is compiled as it lies.
+        hdr = OUT / "ref_p87_fp32_dispatch.h"
+        hdr.write_text(
+            "#pragma once\n#include <torch/extension.h>\n"
+            "#undef AT_DISPATCH_FLOATING_TYPES_AND2\n"
+            "#define AT_DISPATCH_FLOATING_TYPES_AND2(T1, T2, TYPE, NAME, ...) "
+            "AT_DISPATCH_SWITCH(TYPE, NAME, AT_DISPATCH_CASE(at::ScalarType::Float, __VA_ARGS__))\n")
+        pre = ["-include", str(hdr)]
     inc = [f"-I{i}" for i in incs]
     nvcc = [str(CUDA_HOME / "bin" / "nvcc"), "-gencode", "arch=compute_100a,code=sm_100a",
              "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-w", "--expt-relaxed-constexpr",
              f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_API_INCLUDE_EXTENSION_H",
              f"-DTORCH_EXTENSION_NAME={name}", "-D__CUDA_NO_HALF_OPERATORS__=0",
-             *inc, "-c", str(src), "-o", str(obj)]
+             *inc, *pre, "-c", str(src), "-o", str(obj)]
     link = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-w", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
             "-DTORCH_API_INCLUDE_EXTENSION_H", *inc, str(shim), str(obj), "-o", str(target),
             f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",

@@ -28,6 +28,9 @@ Operator semantics (reference file:line):
   A^T B (A stored (K,M))                            kernels/16_...:124
   A B^T (B stored (N,K))                            kernels/17_...:267
   A^T B^T                                           kernels/18_...:152
+  pointwise conv: out[n,o,h,w] = sum_c W[o,c] x[n,c,h,w] + bias[o]
+         (K87 accumulates over in_channels, :340, then adds the bias,
+         :374-386)                                  kernels/87_...:451
 """
 from __future__ import annotations
 
@@ -100,11 +103,26 @@ def transposed_both(A, B):
     return _f64(A).T @ _f64(B).T
 
 
+def pointwise_conv(x, weight, bias=None):
+    """out (N, Cout, H, W) = 1x1 conv of x (N, Cin, H, W)   kernels/87_...:451
+
+    weight is (Cout, Cin) or (Cout, Cin, 1, 1); bias (Cout,) or None.
+    """
+    x = _f64(x)
+    w = _f64(weight).reshape(weight.shape[0], -1)
+    n, c, h, wd = x.shape
+    out = np.einsum("oc,ncs->nos", w, x.reshape(n, c, h * wd))
+    if bias is not None:
+        out = out + _f64(bias).reshape(1, -1, 1)
+    return out.reshape(n, w.shape[0], h, wd)
+
+
 BY_PID = {
     4: gemv, 5: matrix_scalar,
     1: square, 2: standard, 3: batched, 6: large_k, 7: small_k, 8: irregular,
     9: tall_skinny, 10: tensor3d, 11: tensor4d, 12: diag, 13: symmetric,
     14: upper_tri, 15: lower_tri, 16: transposed_a, 17: transposed_b, 18: transposed_both,
+    87: pointwise_conv,
 }
 
 

@@ -70,6 +70,17 @@ cases.append({"pid": 4, "name": "gemv", "A": [[1.0, 2.0, 3.0], [4.0, 5.0, 6.0]],
 cases.append({"pid": 5, "name": "scalar", "A": [[1.0, -2.0], [0.5, 3.0]], "B": 4.0,
               "C": [[4.0, -8.0], [2.0, 12.0]]})
 
+# Pointwise conv, input (1, 2, 2, 2): channel 0 = [[1,2],[3,4]], channel 1 = [[5,6],[7,8]];
+# weight (3, 2, 1, 1) rows [1,0], [0,1], [1,-1]; bias [0.5, -1, 2]:
+# out channel 0 = x0 + 0.5, channel 1 = x1 - 1, channel 2 = x0 - x1 + 2 = -2 everywhere.
+x0, x1 = [[1.0, 2.0], [3.0, 4.0]], [[5.0, 6.0], [7.0, 8.0]]
+wt = [[[[1.0]], [[0.0]]], [[[0.0]], [[1.0]]], [[[1.0]], [[-1.0]]]]
+cases.append({"pid": 87, "name": "conv1x1_bias", "A": [[x0, x1]], "B": wt, "bias": [0.5, -1.0, 2.0],
+              "C": [[[[1.5, 2.5], [3.5, 4.5]], [[4.0, 5.0], [6.0, 7.0]],
+                     [[-2.0, -2.0], [-2.0, -2.0]]]]})
+cases.append({"pid": 87, "name": "conv1x1_nobias", "A": [[x0, x1]], "B": wt,
+              "C": [[x0, x1, [[-4.0, -4.0], [-4.0, -4.0]]]]})
+
 out = Path(__file__).with_name("known_answers.json")
 out.write_text(json.dumps({"cases": cases}, indent=0))
 print(f"wrote {len(cases)} cases to {out}")

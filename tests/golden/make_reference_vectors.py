@@ -6,7 +6,7 @@ draws small seeded N(0,1) inputs on the CPU (torch.Generator, so the test
 can regenerate them bit-for-bit), runs the reference's Part-3 function and
 stores its output (row subsets for the larger ones).  Shapes stay inside
 each reference kernel's own contract (tile multiples, K7's K = 64, K9's
-inner dimension <= 32, K16's block swizzle needing M and N multiples of 512,
+inner dimension <= 32, K87's channel and tile multiples, K16's block swizzle needing M and N multiples of 512,
 kernels/16_Matmul_with_transposed_A_best_kernel.cu:18-40).  K2 is skipped: its shape is hard-coded
 (kernels/2_Standard_matrix_multiplication_best_kernel.cu:16-18).  K4 is
 not run: its first call here (M = 96, K = 1024) raised an illegal memory
@@ -45,6 +45,11 @@ CASES = {
     16: ([(64, 512), (64, 512)], 64),     # K16's 8x8 block swizzle needs M, N % 512
     17: ([(128, 64), (96, 64)], 64),
     18: ([(64, 64), (256, 64)], 64),
+    # K87: input (N, Cin, H, W), weight (Cout, Cin, 1, 1), bias (Cout,).  Its
+    # contract (kernels/87_conv_pointwise_2D_best_kernel.cu:183-330): unguarded
+    # 8-wide weight loads need Cout % 128 == 0 and Cin % 8 == 0, 8-wide input
+    # loads need H*W % 8 == 0, and full 64-position tiles N*H*W % 64 == 0.
+    87: ([(2, 40, 4, 16), (128, 40, 1, 1), (128,)], None),
 }
 SEED0 = 1234
 
@@ -70,8 +75,8 @@ def main():
     out = {}
     for pid, (_, keep) in CASES.items():
         f = build_ref.load(pid)
-        A, B = inputs(pid)
-        C = f(A.cuda(), B if pid == 5 else B.cuda())
+        A, B, *rest = inputs(pid)
+        C = f(A.cuda(), B if pid == 5 else B.cuda(), *[t.cuda() for t in rest])
         torch.cuda.synchronize()
         C = C.cpu().numpy()
         if keep is not None:

@@ -18,7 +18,8 @@ def _cases():
 def test_known_answers(case):
     f = O.BY_PID[case["pid"]]
     B = case["B"] if case["pid"] == 5 else np.array(case["B"], dtype=np.float32)
-    got = f(np.array(case["A"], dtype=np.float32), B)
+    extra = [np.array(case["bias"], dtype=np.float32)] if "bias" in case else []
+    got = f(np.array(case["A"], dtype=np.float32), B, *extra)
     np.testing.assert_array_equal(np.asarray(got, dtype=np.float64), np.array(case["C"]))
 
 
