@@ -24,6 +24,29 @@
 #include "../../include/b2g_gemm.h"
 #include "gemm_engine.cuh"
 
+// Output-bound short-K units (at most B2G_SHORTK_KB K blocks): operand
+// stages and staging boxes per epilogue warp, CTA pair / single CTA.
+#ifndef B2G_SHORTK_KB
+#define B2G_SHORTK_KB 0
+#endif
+#ifndef B2G_SHORTK_STAGES
+#define B2G_SHORTK_STAGES 3
+#endif
+#ifndef B2G_SHORTK_EPIG
+#define B2G_SHORTK_EPIG 4
+#endif
+#ifndef B2G_SHORTK_STAGES1
+#define B2G_SHORTK_STAGES1 2
+#endif
+#ifndef B2G_SHORTK_EPIG1
+#define B2G_SHORTK_EPIG1 4
+#endif
+#ifndef B2G_DYNAMIC_UNITS
+#define B2G_DYNAMIC_UNITS 1    // hand out work units dynamically (plain GEMMs)
+#endif
+#ifndef B2G_NONPERSIST_KB
+#define B2G_NONPERSIST_KB 0
+#endif
 #ifndef B2G_PAIR256_STAGES
 #define B2G_PAIR256_STAGES 6   // pipeline depth of the CTA-pair 256-wide engine
 #endif
@@ -95,6 +118,30 @@ int take_injected_stall() {
   }
   int one = 1;
   return armed.compare_exchange_strong(one, 0) ? 1 : 0;
+}
+
+// ------------------------------------------------------- dynamic unit schedule
+// Counter pairs of the dynamic schedule (EngineParams::sched), one per launch
+// taken round-robin from a file-scope array: zero at module load, and each
+// launch leaves its pair at zero when it ends.  Launches that share a slot
+// are kSchedSlots launches apart, so never run at the same time.
+constexpr int kSchedSlots = 4096;
+static __device__ unsigned long long g_sched[kSchedSlots][2];
+
+unsigned long long* sched_slot() {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<unsigned long long*> base[kMaxDevices];
+  static std::atomic<unsigned> next{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  unsigned long long* b = base[dev].load();
+  if (!b) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_sched) != cudaSuccess) return nullptr;
+    b = static_cast<unsigned long long*>(addr);
+    base[dev].store(b);
+  }
+  return b + 2 * (next.fetch_add(1) % kSchedSlots);
 }
 
 // ---------------------------------------------------------------- tensor maps
@@ -554,9 +601,13 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
     // L2 and shared memory, which costs power and so clock under the 1 kW
     // cap.  The 512-wide pair unit (no accumulator double buffering) pays
     // off only when a unit's K loop is long enough to hide its epilogue.
-    struct Cand { int ctas, bn; double eff, eff_long_k; };
-    const Cand cands[] = {{2, 256, 1.0, 1.0}, {2, 512, 0.85, 1.05}, {1, 256, 0.83, 0.83},
-                          {2, 128, 0.66, 0.66}, {1, 128, 0.63, 0.63}};
+    // Units of at most two K blocks are output-bound: there single-CTA units
+    // store faster than pairs (16384^2 x 32: 6.49 / 5.07 / 4.83 / 3.60 TB/s
+    // for single256 / single128 / pair256 / pair128).
+    struct Cand { int ctas, bn; double eff, eff_long_k, eff_short_k; };
+    const Cand cands[] = {{2, 256, 1.0, 1.0, 1.0}, {2, 512, 0.85, 1.05, 0.85},
+                          {1, 256, 0.83, 0.83, 1.34}, {2, 128, 0.66, 0.66, 0.75},
+                          {1, 128, 0.63, 0.63, 1.05}};
     // B2G_TILE=pair512|pair256|pair128|single256|single128 pins the choice
     // (a tuning and test aid).
     double best = 0.0;
@@ -570,7 +621,7 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
       int64_t splits, kbps;
       choose_splits(d, units * c.ctas, kb_total, num_sms, &splits, &kbps);
       const double waves = static_cast<double>(cdiv(units * splits * c.ctas, num_sms));
-      const double eff = kbps >= 64 ? c.eff_long_k : c.eff;
+      const double eff = kbps >= 64 ? c.eff_long_k : (kbps <= 2 ? c.eff_short_k : c.eff);
       const double cost = waves * c.bn * static_cast<double>(std::max<int64_t>(kbps, 1)) / eff;
       if (best == 0.0 || cost < best * 0.999) {
         best = cost;
@@ -600,6 +651,9 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   pl->kb_per_split = static_cast<int32_t>(kbps);
   pl->work_units = tiles * splits;
   pl->grid = static_cast<int32_t>(std::min<int64_t>(pl->work_units, num_sms / ctas) * ctas);
+  if (B2G_NONPERSIST_KB > 0 && kb_total <= B2G_NONPERSIST_KB && d->op == B2G_OP_GEMM && !x3 &&
+      splits == 1)
+    pl->grid = static_cast<int32_t>(std::min<int64_t>(pl->work_units, 1 << 20) * ctas);
   pl->a_mn_major = d->trans_a ? 1 : 0;
   pl->b_mn_major = d->trans_b ? 0 : 1;
   pl->tma_store = (reinterpret_cast<uintptr_t>(d->c) % 16 == 0) && (d->ldc % 4 == 0) &&
@@ -775,6 +829,13 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.diag_oob_row = static_cast<int>(d->m);
   p.row_bias = row_bias;
   p.err = err_word;
+  // Dynamic schedule: plain GEMMs with more units than CTAs (pairs), every
+  // unit holding at least one K block (no structurally empty units).
+  const int64_t slots = pl.grid / pl.cluster_ctas;
+  if (B2G_DYNAMIC_UNITS && d->op == B2G_OP_GEMM && d->k > 0 && pl.work_units > slots &&
+      static_cast<int64_t>(pl.splits - 1) * pl.kb_per_split < p.kb_total) {
+    p.sched = sched_slot();
+  }
 
   if (p.atomic_out) {
     // Split-K accumulates into C: clear it first.
@@ -854,6 +915,15 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     return launch_majors<256, 6, false, true, true>(a_mn, b_mn, maps, p, grid, stream);
   if (tri_xf)
     return launch_majors<128, 6, false, true, false>(a_mn, b_mn, maps, p, grid, stream);
+  if (B2G_SHORTK_KB > 0 && p.kb_total <= B2G_SHORTK_KB && !p.atomic_out && pl.tma_store) {
+    // Output-bound short-K units: few operand stages, a ring of staging boxes.
+    if (B2G_SHORTK_EPIG > 1 && pl.cluster_ctas == 2 && pl.block_n == 256)
+      return launch_majors<256, B2G_SHORTK_STAGES, false, false, true, B2G_SHORTK_EPIG>(
+          a_mn, b_mn, maps, p, grid, stream);
+    if (B2G_SHORTK_EPIG1 > 1 && pl.cluster_ctas == 1 && pl.block_n == 256)
+      return launch_majors<256, B2G_SHORTK_STAGES1, false, false, false, B2G_SHORTK_EPIG1>(
+          a_mn, b_mn, maps, p, grid, stream);
+  }
   if (pl.cluster_ctas == 2) {
     if (pl.block_n == 512)
       return launch_majors<512, 4, false, false, true>(a_mn, b_mn, maps, p, grid, stream);

@@ -42,6 +42,7 @@ enum : int {
   kErrWaitTmemEmpty = 0x104,
   kErrWaitTmemFull = 0x105,
   kErrWaitXform = 0x106,
+  kErrWaitUnit = 0x107,
 };
 
 struct EngineParams {
@@ -67,7 +68,39 @@ struct EngineParams {
   const int4* unit_table;      // if set: unit w is {tm, tn, kb_lo, kb_hi | flags << 24}
   int diag_oob_row;            // a K row past every operand row (zero-filled by TMA)
   const float* row_bias;       // if set: C[b][i][j] += row_bias[i] (added by the K piece at 0)
+  // If set: units are handed out dynamically.  sched[0] counts units drawn
+  // past each CTA (pair)'s first, sched[1] the CTAs (pairs) done drawing; the
+  // last one to finish resets both to 0 for the next launch.  Only for work
+  // in which every unit has at least one K block.
+  unsigned long long* sched;
   int* err;
+};
+
+// Depth of the per-CTA ring through which the pair leader's producer hands
+// dynamically drawn unit indices to every role of both CTAs.  A role can
+// lag the producer by at most STAGES + 2 units (operand stages, then
+// accumulator buffers, each unit holding >= 1 K block), far below it.
+constexpr int kUnitQueue = 32;
+
+// The sequence of units a CTA (pair) runs: unit0, unit0 + step, ... when
+// static; the ring's entries, in order, when dynamic.  get() returns false
+// when a bounded wait gave up.
+struct UnitSource {
+  uint64_t* bars;
+  long long* slots;
+  long long unit0, step;
+  bool dyn;
+  __device__ __forceinline__ bool get(uint32_t i, long long& w, volatile int* abort,
+                                      uint64_t limit_ns) const {
+    if (!dyn) {
+      w = unit0 + static_cast<long long>(i) * step;
+      return true;
+    }
+    const int q = static_cast<int>(i % kUnitQueue);
+    if (!ptx::mbar_wait_cluster(&bars[q], (i / kUnitQueue) & 1, abort, limit_ns)) return false;
+    w = *reinterpret_cast<volatile long long*>(&slots[q]);
+    return true;
+  }
 };
 
 struct WorkUnit {
@@ -208,13 +241,17 @@ struct EngineCfg {
   static constexpr int kEpiParts = EPIW / 4;
   static_assert(EPIW % 4 == 0 && EPIW >= 4, "epilogue warps come in quadrant sets");
   static constexpr int kEpiBufBytes = 32 * 32 * 4;           // one 32 x 32 fp32 box
-  static constexpr int kEpiBufs = EPIG;                      // staging boxes per epilogue warp
-  static constexpr int kEpiGroup = EPIG;                     // chunks staged per fence
+  // Staging boxes per epilogue warp.  One: each chunk waits for the previous
+  // store to have read the box.  More: a ring, up to EPIG - 1 stores of the
+  // warp still reading while the next box is written (output-bound shapes).
+  static constexpr int kEpiBufs = EPIG;
+  static constexpr int kEpiGroup = 1;                        // chunks staged per fence
   static constexpr int kEpiBytes = kEpiWarps * kEpiBufs * kEpiBufBytes;
   static constexpr int kOffBar = kOffEpi + kEpiBytes;
   static constexpr int kNumBars = 3 * STAGES + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr int kSmemBytes = kOffMisc + 16 + 1024;   // + alignment slack
+  static constexpr int kOffQueue = kOffMisc + 16;            // unit ring: barriers, then slots
+  static constexpr int kSmemBytes = kOffQueue + kUnitQueue * 16 + 1024;   // + alignment slack
   static constexpr int kAccBufs = BN > 256 ? 1 : 2;         // accumulator buffers in TMEM
   static constexpr int kTmemCols = kAccBufs * BN;
   static constexpr int kXformWarps = XF ? 4 : 0;
@@ -356,7 +393,7 @@ __device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[32]) {
 template <int NBUF>
 __device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtensorMap* map_c,
                                             float* stg, uint32_t& seq, uint32_t (&r)[32], int b,
-                                            int row0, int col0, int lane) {
+                                            int row0, int col0, int lane, int accumulate) {
   const int row = row0 + lane;
   if (p.tri == kTriUpper) {
 #pragma unroll
@@ -381,7 +418,7 @@ __device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtenso
     ptx::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      if (p.atomic_out)
+      if (p.atomic_out || accumulate)
         ptx::tma_reduce_add_3d(map_c, buf, col0, row0, b);
       else
         ptx::tma_store_3d(map_c, buf, col0, row0, b);
@@ -489,6 +526,12 @@ __global__ void __launch_bounds__(
   const bool leader = rank == 0;
   const long long unit0 = PAIR ? (blockIdx.x >> 1) : blockIdx.x;
   const long long unit_step = PAIR ? (gridDim.x >> 1) : gridDim.x;
+  UnitSource units;
+  units.bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffQueue);
+  units.slots = reinterpret_cast<long long*>(smem + Cfg::kOffQueue + kUnitQueue * 8);
+  units.unit0 = unit0;
+  units.step = unit_step;
+  units.dyn = p.sched != nullptr;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -501,6 +544,7 @@ __global__ void __launch_bounds__(
       ptx::mbar_init(&tmem_empty[b], Cfg::kEpiWarps * Cfg::kCtas);
     }
     ptx::mbar_init(mma_drain, 1);
+    for (int q = 0; q < kUnitQueue; ++q) ptx::mbar_init(&units.bars[q], 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -532,9 +576,28 @@ __global__ void __launch_bounds__(
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint32_t full_leader = PAIR ? ptx::mapa_shared(ptx::smem_addr(full), 0) : 0u;
+      // The pair leader's producer draws the units (dynamic schedule) and
+      // publishes each to both CTAs' rings; every other role reads a ring.
+      const bool fetcher = units.dyn && leader;
       uint32_t it = 0;
       bool ok = true;
-      for (long long w = unit0; w < p.work_units && ok; w += unit_step) {
+      for (uint32_t ui = 0; ok; ++ui) {
+        long long w;
+        if (fetcher) {
+          w = ui == 0 ? unit0 : unit_step + static_cast<long long>(atomicAdd(p.sched, 1ull));
+          const int q = static_cast<int>(ui % kUnitQueue);
+          *reinterpret_cast<volatile long long*>(&units.slots[q]) = w;
+          ptx::mbar_arrive(&units.bars[q]);
+          if (PAIR) {
+            ptx::st_shared_cluster_u64(ptx::mapa_shared(ptx::smem_addr(&units.slots[q]), 1),
+                                       static_cast<uint64_t>(w));
+            ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&units.bars[q]), 1));
+          }
+        } else if (!units.get(ui, w, abort_flag, p.wait_limit_ns)) {
+          record_error(p.err, abort_flag, kErrWaitUnit);
+          break;
+        }
+        if (w >= p.work_units) break;
         const WorkUnit u = decode_unit(p, w);
         const int m_cta = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM;
         // B sub-tile j of this CTA: columns [n0 + j*kMmaN + rank*kSubCols, +kSubCols)
@@ -655,6 +718,15 @@ __global__ void __launch_bounds__(
           }
         }
       }
+      if (fetcher) {
+        // Done drawing: the last CTA (pair) to get here resets the counters
+        // for the next launch (every other one has drawn its last unit).
+        __threadfence();
+        if (atomicAdd(p.sched + 1, 1ull) == static_cast<unsigned long long>(unit_step - 1)) {
+          atomicExch(p.sched, 0ull);
+          atomicExch(p.sched + 1, 0ull);
+        }
+      }
       // Drain: the bytes of every stage issued must land before the CTA may
       // exit, also when another role gave up early (bounded; a no-op on the
       // normal path, where the MMA warp already waited for each of them).
@@ -685,7 +757,13 @@ __global__ void __launch_bounds__(
       constexpr uint32_t b_kstep = B_MN ? 8 * kSwRowBytes : 8 * 4;
       uint32_t it = 0, tl = 0;
       bool ok = true;
-      for (long long w = unit0; w < p.work_units && ok; w += unit_step) {
+      for (uint32_t ui = 0; ok; ++ui) {
+        long long w;
+        if (!units.get(ui, w, abort_flag, p.wait_limit_ns)) {
+          record_error(p.err, abort_flag, kErrWaitUnit);
+          break;
+        }
+        if (w >= p.work_units) break;
         const WorkUnit u = decode_unit(p, w);
         if (u.kb_lo >= u.kb_hi) continue;
         const int buf = tl % Cfg::kAccBufs;
@@ -776,7 +854,13 @@ __global__ void __launch_bounds__(
     const uint32_t tmem_empty_leader =
         PAIR ? ptx::mapa_shared(ptx::smem_addr(tmem_empty), 0) : 0u;
     uint32_t tl = 0, seq = 0;
-    for (long long w = unit0; w < p.work_units; w += unit_step) {
+    for (uint32_t ui = 0;; ++ui) {
+      long long w;
+      if (!units.get(ui, w, abort_flag, p.wait_limit_ns)) {
+        if (lane == 0) record_error(p.err, abort_flag, kErrWaitUnit);
+        break;
+      }
+      if (w >= p.work_units) break;
       const WorkUnit u = decode_unit(p, w);
       const int row0 = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM + quad * 32;
       const int n0 = u.tn * BN;
@@ -841,7 +925,7 @@ __global__ void __launch_bounds__(
       // Row bias (this lane's output row), added once: by the K piece that starts at 0.
       const bool with_bias = p.row_bias != nullptr && u.kb_lo == 0;
       const float bias_v = (with_bias && row0 + lane < p.M) ? p.row_bias[row0 + lane] : 0.f;
-      if (row0 < p.M && half < nch && p.tma_store) {
+      if (row0 < p.M && half < nch && p.tma_store && Cfg::kEpiBufs == 1) {
         // TMA path: groups of kEpiGroup chunks, one TMEM wait and one fence each.
         constexpr int G = Cfg::kEpiGroup;
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
@@ -887,7 +971,8 @@ __global__ void __launch_bounds__(
 #pragma unroll
             for (int i = 0; i < 32; ++i) ra[i] = __float_as_uint(__uint_as_float(ra[i]) + bias_v);
           }
-          store_chunk<Cfg::kEpiBufs>(p, &map_c, stg, seq, ra, u.b, row0, n0 + ch * 32, lane);
+          store_chunk<Cfg::kEpiBufs>(p, &map_c, stg, seq, ra, u.b, row0, n0 + ch * 32, lane,
+                                     u.accumulate);
           if (more) {
             tmem_ld_wait_regs(rb);
 #pragma unroll
@@ -908,7 +993,13 @@ __global__ void __launch_bounds__(
     const uint32_t ready_leader = PAIR ? ptx::mapa_shared(ptx::smem_addr(ready), 0) : 0u;
     uint32_t it = 0;
     bool ok = true;
-    for (long long w = unit0; w < p.work_units && ok; w += unit_step) {
+    for (uint32_t ui = 0; ok; ++ui) {
+      long long w;
+      if (!units.get(ui, w, abort_flag, p.wait_limit_ns)) {
+        if (lane == 0) record_error(p.err, abort_flag, kErrWaitUnit);
+        break;
+      }
+      if (w >= p.work_units) break;
       const WorkUnit u = decode_unit(p, w);
       const int m0 = u.tm * Cfg::kUnitM + static_cast<int>(rank) * kBlockM;
       const int n0 = u.tn * BN + static_cast<int>(rank) * Cfg::kSubCols;

@@ -95,6 +95,39 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
                : "memory");
 }
 
+// As mbar_try_wait with acquire at cluster scope: pairs with an arrive.release.cluster
+// made by another CTA of the cluster, so that CTA's earlier stores are visible.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait as mbar_wait, with cluster-scope acquire.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort, uint64_t limit_ns) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// 64-bit store to a shared::cluster address (any CTA of the cluster).
+__device__ __forceinline__ void st_shared_cluster_u64(uint32_t cluster_addr, uint64_t v) {
+  asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(cluster_addr), "l"(v) : "memory");
+}
+
 // As mbar_wait, for waits expected to be long (an epilogue waiting out a
 // whole mainloop): after a short spin, back off with nanosleep between
 // probes so idle warps stop competing for issue slots and power.

@@ -84,6 +84,16 @@ def test_plan_grid_is_even_for_pairs(capi):
             assert p.grid % 2 == 0 and p.grid <= 148
 
 
+def test_plan_short_k_prefers_single_cta_units(capi):
+    # Output-bound (K <= 64): single-CTA 128 x 256 units store faster than pairs.
+    for m, n, k in [(16384, 16384, 32), (16384, 16384, 64)]:
+        p = _plan(capi, m, n, k)
+        assert p.cluster_ctas == 1 and p.block_n == 256 and p.splits == 1
+    # A longer K loop keeps the pair.
+    p = _plan(capi, 16 * 256 * 512, 768, 256)
+    assert p.cluster_ctas == 2
+
+
 def test_plan_unaligned_output_disables_tma_store(capi):
     p = _plan(capi, 100, 101, 64, ldc=101)
     assert p.tma_store == 0
