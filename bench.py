@@ -516,6 +516,9 @@ def shape_table(W, peaks, only, ops):
         op = ops.OPERATORS[w.pid].forward
         row = {"pid": w.pid, "shapes": w.shapes}
         ours = lambda: op(*args)
+        # Let SM clocks recover from the previous (possibly power-capped) shape.
+        torch.cuda.synchronize()
+        time.sleep(0.5)
         k = adaptive_steps(ours)
         _, ms = time_loop(ours, k, 3)
         row["ours"] = roofline(w, ms, peaks)
