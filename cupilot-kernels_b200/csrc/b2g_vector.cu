@@ -95,12 +95,26 @@ __global__ void __launch_bounds__(256) gemv_block_rows_kernel(const float* __res
 }
 
 // out[i] = a[i] * s, one rounding per element.
+// out = a * s over float4s: each thread issues kScaleUnroll independent
+// 16-byte streaming loads (a block's loads cover 4 KB per step) before its
+// stores, so enough bytes are in flight per SM to cover HBM latency.
+constexpr int kScaleUnroll = 4;
 __global__ void __launch_bounds__(256) scale_vec_kernel(const float4* __restrict__ a, float s,
                                                         float4* __restrict__ out, int64_t n4) {
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const float4 v = __ldcs(a + i);
-    __stcs(out + i, make_float4(v.x * s, v.y * s, v.z * s, v.w * s));
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x * kScaleUnroll;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x * kScaleUnroll + threadIdx.x;
+       base < n4; base += step) {
+    float4 v[kScaleUnroll];
+#pragma unroll
+    for (int u = 0; u < kScaleUnroll; ++u) {
+      const int64_t i = base + static_cast<int64_t>(u) * blockDim.x;
+      if (i < n4) v[u] = __ldcs(a + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kScaleUnroll; ++u) {
+      const int64_t i = base + static_cast<int64_t>(u) * blockDim.x;
+      if (i < n4) __stcs(out + i, make_float4(v[u].x * s, v[u].y * s, v[u].z * s, v[u].w * s));
+    }
   }
 }
 
@@ -157,7 +171,7 @@ extern "C" int b2g_scale(const float* a, float s, float* out, int64_t n,
                    (reinterpret_cast<uintptr_t>(out) % 16 == 0);
   const int64_t n4 = vec ? n / 4 : 0;
   if (n4 > 0) {
-    const int64_t blocks = std::min<int64_t>(cdiv(n4, 256), static_cast<int64_t>(sm_count()) * 16);
+    const int64_t blocks = std::min<int64_t>(cdiv(n4, 256 * kScaleUnroll), int64_t{1} << 30);
     scale_vec_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
         reinterpret_cast<const float4*>(a), s, reinterpret_cast<float4*>(out), n4);
   }

@@ -247,6 +247,9 @@ struct EngineCfg {
   static constexpr int kEpiBufs = EPIG;
   static constexpr int kEpiGroup = 1;                        // chunks staged per fence
   static constexpr int kEpiBytes = kEpiWarps * kEpiBufs * kEpiBufBytes;
+  // A CTA's last unit stages its output in the idle operand stages instead:
+  // a ring of this many boxes per epilogue warp, so its stores overlap.
+  static constexpr int kTailBoxes = kOffEpi / (kEpiWarps * kEpiBufBytes);
   static constexpr int kOffBar = kOffEpi + kEpiBytes;
   static constexpr int kNumBars = 3 * STAGES + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
@@ -452,7 +455,7 @@ __device__ __forceinline__ void store_chunk(const EngineParams& p, const CUtenso
 // global memory through G swizzled staging boxes: one wait for the previous
 // group's stores to have read the boxes, one proxy fence, G tensor stores
 // (or fp32 add-reductions for split-K).
-template <int G>
+template <int G, int PENDING = 0>
 __device__ __forceinline__ void store_group_tma(const EngineParams& p, const CUtensorMap* map_c,
                                                 float* stg, uint32_t (&r)[G][32], int ng, int b,
                                                 int row0, const int (&col0)[G], int lane,
@@ -467,7 +470,9 @@ __device__ __forceinline__ void store_group_tma(const EngineParams& p, const CUt
         if (p.tri == kTriUpper ? (col < row) : (col > row)) r[g][j] = 0u;
       }
   }
-  if (lane == 0) ptx::bulk_wait_read<0>();
+  // Staging boxes reused: wait until at most PENDING earlier store groups
+  // of this warp may still be reading theirs (0: a single box).
+  if (lane == 0) ptx::bulk_wait_read<PENDING>();
   __syncwarp();
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -925,9 +930,22 @@ __global__ void __launch_bounds__(
       // Row bias (this lane's output row), added once: by the K piece that starts at 0.
       const bool with_bias = p.row_bias != nullptr && u.kb_lo == 0;
       const float bias_v = (with_bias && row0 + lane < p.M) ? p.row_bias[row0 + lane] : 0.f;
+      // Last unit of this CTA (pair): every MMA has read its operands and no
+      // load will follow, so the operand stages are free for staging.
+      bool tail = false;
+      if (Cfg::kTailBoxes >= 2 && p.tma_store && Cfg::kEpiBufs == 1) {
+        long long w_next;
+        if (!units.get(ui + 1, w_next, abort_flag, p.wait_limit_ns)) {
+          if (lane == 0) record_error(p.err, abort_flag, kErrWaitUnit);
+          break;
+        }
+        tail = w_next >= p.work_units;
+      }
       if (row0 < p.M && half < nch && p.tma_store && Cfg::kEpiBufs == 1) {
         // TMA path: groups of kEpiGroup chunks, one TMEM wait and one fence each.
         constexpr int G = Cfg::kEpiGroup;
+        constexpr int kTail = Cfg::kTailBoxes >= 2 ? Cfg::kTailBoxes : 2;
+        float* tail_stg = reinterpret_cast<float*>(smem) + ew * kTail * 32 * 32;
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
         const int mine = (nch - half + kParts - 1) / kParts;   // chunks half, half+kParts, ...
 #pragma unroll 1
@@ -953,7 +971,11 @@ __global__ void __launch_bounds__(
               for (int i = 0; i < 32; ++i) r[g][i] = __float_as_uint(__uint_as_float(r[g][i]) + bias_v);
           }
           if (g0 + G >= mine) release();                      // every TMEM read is done
-          store_group_tma<G>(p, &map_c, stg, r, ng, u.b, row0, col0, lane, u.accumulate);
+          if (tail)
+            store_group_tma<G, kTail - 1>(p, &map_c, tail_stg + ((g0 / G) % kTail) * G * 32 * 32,
+                                          r, ng, u.b, row0, col0, lane, u.accumulate);
+          else
+            store_group_tma<G>(p, &map_c, stg, r, ng, u.b, row0, col0, lane, u.accumulate);
         }
       } else if (row0 < p.M && half < nch) {
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
