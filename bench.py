@@ -225,6 +225,9 @@ def device_inputs(w, seed_offset=0, **shapes):
     if n == "pointwise_conv":
         return (r(s["batch"], s["cin"], s["h"], s["w"]), r(s["cout"], s["cin"], 1, 1),
                 r(s["cout"]))
+    if n == "sdpa":
+        shape = (s["batch"], s["heads"], s["seq"], s["dim"])
+        return tuple(r(*shape).half() for _ in range(3))
     raise KeyError(n)
 
 
@@ -232,6 +235,8 @@ def cublas_fn(name, A, B, *rest):
     """The same math through torch (cuBLAS TF32) for the comparison column."""
     if name == "pointwise_conv":   # cuDNN conv2d (TF32 allowed by default)
         return lambda: torch.nn.functional.conv2d(A, B, rest[0])
+    if name == "sdpa":             # torch's fused attention (backend of its choice)
+        return lambda: torch.nn.functional.scaled_dot_product_attention(A, B, rest[0])
     if name == "transposed_a":
         return lambda: torch.matmul(A.t(), B)
     if name == "transposed_b":
@@ -256,13 +261,15 @@ def roofline(w, ms, peaks, flops=None, nbytes=None):
     s = ms / 1e3
     tflops = flops / s / 1e12
     gbs = nbytes / s / 1e9
-    t_c = flops / (peaks["tf32_tflops"] * 1e12)
+    # fp16 operands (attention) run at the f16 tensor rate, the rest at TF32's.
+    tpeak = peaks["bf16_tflops"] if w.name == "sdpa" else peaks["tf32_tflops"]
+    t_c = flops / (tpeak * 1e12)
     t_m = nbytes / (peaks["hbm_gbs"] * 1e9)
     if w.bound == "hbm" or t_m > t_c:
         return {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4), "tflops": round(tflops, 2)}
-    return {"bound": "tensor", "achieved": round(tflops, 2), "peak": round(peaks["tf32_tflops"], 1),
-            "unit": "TFLOP/s", "frac": round(tflops / peaks["tf32_tflops"], 4),
+    return {"bound": "tensor", "achieved": round(tflops, 2), "peak": round(tpeak, 1),
+            "unit": "TFLOP/s", "frac": round(tflops / tpeak, 4),
             "gbs": round(gbs, 1)}
 
 
@@ -272,7 +279,7 @@ REF_SAFE = {  # workload -> reference PID whose kernel runs on the workload
     "square": 1, "batched": 3, "large_k": 6, "small_k": 7, "irregular": 8, "tall_skinny": 9,
     "tensor3d": 10, "tensor4d": 11, "diag": 12, "symmetric": 13, "upper_tri": 14,
     "lower_tri": 15, "transposed_a": 16, "transposed_b": 17, "transposed_both": 18,
-    "pointwise_conv": 87,
+    "pointwise_conv": 87, "sdpa": 97,
 }
 
 
@@ -295,6 +302,8 @@ def reference_callable(name, A, B, *rest):
         return (lambda: f(A, B)), "as is; K9 uses only 32 of the 64 inner columns (parity FAIL)"
     if name == "pointwise_conv":
         return (lambda: f(A, B, rest[0])), "float32 dispatch only (its double instance fails ptxas)"
+    if name == "sdpa":
+        return (lambda: f(A, B, rest[0])), None
     return (lambda: f(A, B)), None
 
 

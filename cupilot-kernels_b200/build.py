@@ -30,7 +30,8 @@ LIB = PKG / "libb2g_sm100.so"
 EXT = PKG / ("_b2g_torch" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 CU_SOURCES = [CSRC / "b2g_capi.cu", CSRC / "b2g_vector.cu"]
-CU_DEPS = CU_SOURCES + [CSRC / "gemm_engine.cuh", CSRC / "ptx_sm100.cuh", INCLUDE / "b2g_gemm.h"]
+CU_DEPS = CU_SOURCES + [CSRC / "gemm_engine.cuh", CSRC / "sdpa_engine.cuh", CSRC / "ptx_sm100.cuh",
+                        INCLUDE / "b2g_gemm.h"]
 EXT_SOURCES = [CSRC / "torch_binding.cpp"]
 
 

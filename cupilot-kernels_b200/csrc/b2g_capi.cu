@@ -23,6 +23,7 @@
 
 #include "../../include/b2g_gemm.h"
 #include "gemm_engine.cuh"
+#include "sdpa_engine.cuh"
 
 // Output-bound short-K units (at most B2G_SHORTK_KB K blocks): operand
 // stages and staging boxes per epilogue warp, CTA pair / single CTA.
@@ -1065,6 +1066,73 @@ extern "C" int b2g_rowscale(const float* d, const float* b, float* out, int64_t 
     if (cudaGetLastError() != cudaSuccess) return B2G_ERR_LAUNCH;
   }
   return B2G_OK;
+}
+
+// ---------------------------------------------------------------- attention
+namespace b2g {
+namespace {
+// fp16 (rows x inner) matrices, nbatch of them rows*inner apart, boxes of
+// 64 (128 bytes, 128-byte swizzle) x box_rows.
+bool make_map_f16(CUtensorMap* map, const void* base, int64_t inner, int64_t rows, int64_t nbatch,
+                  uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(nbatch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(inner) * 2,
+                           static_cast<cuuint64_t>(inner * rows) * 2};
+  cuuint32_t box[3] = {64, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+}  // namespace b2g
+
+extern "C" int b2g_sdpa(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                        int64_t heads, int64_t seq, int64_t dim, float scale,
+                        b2g_stream_t stream_handle) {
+  if (batch < 0 || heads < 0 || seq < 0 || dim < 0) return B2G_ERR_INVALID_ARG;
+  const int64_t bh = batch * heads;
+  if (bh == 0 || seq == 0 || dim == 0) return B2G_OK;
+  if (!q || !k || !v || !out) return B2G_ERR_INVALID_ARG;
+  if (seq > sdpa::kKeysMax || dim % 64 != 0 || bh > (1ll << 30) || dim * seq > (1ll << 30))
+    return B2G_ERR_UNSUPPORTED;
+  for (const void* ptr : {q, k, v, static_cast<const void*>(out)})
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return B2G_ERR_UNSUPPORTED;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  DeviceState* ds = nullptr;
+  int rc = device_state(&ds);
+  if (rc != B2G_OK) return rc;
+  CUtensorMap mq, mk, mv;
+  if (!make_map_f16(&mq, q, dim, seq, bh, sdpa::kBM) ||
+      !make_map_f16(&mk, k, dim, seq, bh, sdpa::kKBox) ||
+      !make_map_f16(&mv, v, dim, seq, bh, sdpa::kVKeys))
+    return B2G_ERR_UNSUPPORTED;
+  sdpa::Params p;
+  p.S = static_cast<int>(seq);
+  p.D = static_cast<int>(dim);
+  p.BH = static_cast<int>(bh);
+  p.qblocks = static_cast<int>(cdiv(seq, sdpa::kBM));
+  p.units = bh * p.qblocks;
+  const float sc = scale > 0.f ? scale : 1.0f / std::sqrt(static_cast<float>(dim));
+  p.scale_log2 = sc * 1.4426950408889634f;
+  p.out = static_cast<__half*>(out);
+  p.wait_limit_ns = wait_limit_ns();
+  p.err = ds->err_word;
+  static thread_local int configured_dev = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_dev != dev) {
+    if (cudaFuncSetAttribute(sdpa::sdpa_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             sdpa::kSmemBytes) != cudaSuccess)
+      return B2G_ERR_LAUNCH;
+    configured_dev = dev;
+  }
+  const int grid = static_cast<int>(std::min<int64_t>(p.units, ds->num_sms));
+  sdpa::sdpa_kernel<<<grid, sdpa::kThreads, sdpa::kSmemBytes, stream>>>(mq, mk, mv, p);
+  return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
 }
 
 extern "C" int b2g_read_device_error(int device, int32_t* code) {

@@ -343,6 +343,28 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
   return d;
 }
 
+// One MMA of kind::f16 (fp16 operands, fp32 accumulator), cta_group::1.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor for kind::f16 with fp16 A and B, fp32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n, bool a_mn_major, bool b_mn_major) {
+  return (1u << 4)                                  // D format: f32
+         | (0u << 7)                                // A format: f16
+         | (0u << 10)                               // B format: f16
+         | (static_cast<uint32_t>(a_mn_major) << 15)
+         | (static_cast<uint32_t>(b_mn_major) << 16)
+         | (static_cast<uint32_t>(n >> 3) << 17)
+         | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
 // Instruction descriptor for kind::tf32, fp32 accumulator, M x N tile.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool a_mn_major,
                                                   bool b_mn_major) {

@@ -329,6 +329,31 @@ at::Tensor pointwise_conv(at::Tensor input, at::Tensor weight, c10::optional<at:
   return out;
 }
 
+// kernels/97_ScaledDotProductAttention_best_kernel.cu:256 (fused_attention_cuda) —
+// out = softmax(Q K^T / sqrt(D)) V for fp16 (batch, heads, seq, dim) tensors.
+at::Tensor fused_attention(at::Tensor Q, at::Tensor K, at::Tensor V) {
+  for (const auto& t : {Q, K, V}) {
+    TORCH_CHECK(t.is_cuda(), "Q, K and V must be CUDA tensors");
+    TORCH_CHECK(t.scalar_type() == at::kHalf, "Q, K and V must be float16");
+    TORCH_CHECK(t.dim() == 4, "Q, K and V must be (batch, heads, seq, dim)");
+  }
+  TORCH_CHECK(K.sizes() == Q.sizes() && V.sizes() == Q.sizes(), "Q, K and V must have one shape");
+  TORCH_CHECK(K.device() == Q.device() && V.device() == Q.device(),
+              "Q, K and V must be on the same device");
+  const int64_t b = Q.size(0), h = Q.size(1), s = Q.size(2), d = Q.size(3);
+  TORCH_CHECK(s <= 512, "Sequence length exceeds 512 (the score row is kept on chip).");
+  TORCH_CHECK(d % 64 == 0, "Embedding dimension must be a multiple of 64.");
+  const c10::cuda::CUDAGuard guard(Q.device());
+  at::Tensor q = Q.contiguous(), k = K.contiguous(), v = V.contiguous();
+  at::Tensor out = at::empty_like(q);
+  if (out.numel() == 0) return out;
+  auto stream = at::cuda::getCurrentCUDAStream(Q.device().index());
+  check_status(b2g_sdpa(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, h, s, d,
+                        0.f, stream.stream()),
+               "b2g_sdpa");
+  return out;
+}
+
 // Generic entry: op(A) . op(B) with explicit flags (used by the partitioner).
 at::Tensor gemm(at::Tensor A, at::Tensor B, bool trans_a, bool trans_b, int64_t op) {
   return matmul_2d(trans_a ? A.t() : A, trans_b ? B.t() : B, static_cast<int>(op));
@@ -369,6 +394,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("matmul_transposed_both", &matmul_transposed_both);
   m.def("gemv", &gemv);
   m.def("matrix_scalar_mult", &matrix_scalar_mult);
+  m.def("fused_attention", &fused_attention, "softmax(Q K^T / sqrt(D)) V, fp16");
   m.def("pointwise_conv", &pointwise_conv, "1x1 convolution, NCHW", py::arg("input"),
         py::arg("weight"), py::arg("bias") = py::none());
   m.def("gemm", &gemm, "op(A) . op(B)", py::arg("A"), py::arg("B"), py::arg("trans_a") = false,

@@ -123,6 +123,9 @@ OPERATORS = {
     # forward(input, weight, bias=None): NCHW 1x1 convolution as a batched GEMM
     87: Operator(87, "pointwise_conv", "pointwise_conv_cuda",
                  _K + "87_conv_pointwise_2D_best_kernel.cu:451", _ext.pointwise_conv),
+    # forward(Q, K, V): fp16 attention, (batch, heads, seq <= 512, dim % 64 == 0)
+    97: Operator(97, "sdpa", "fused_attention_cuda",
+                 _K + "97_ScaledDotProductAttention_best_kernel.cu:256", _ext.fused_attention),
 }
 
 for _pid, _op in OPERATORS.items():

@@ -179,6 +179,21 @@ _add(_w("pointwise_conv", 87, dict(batch=16, cin=64, cout=128, h=256, w=256), 17
         _conv_cost(16, 64, 128, 256, 256), "hbm"))
 
 
+# Next row (reference PID 97): attention, fp16.  The reference kernel only
+# runs at seq 512 and dim 1024 (kernels/97_ScaledDotProductAttention_best_kernel.cu:9-10);
+# batch and heads are chosen: 8 x 16 heads, 128 MB per tensor.
+def _mk_sdpa(g, batch, heads, seq, dim):
+    return tuple(_randn(g, batch, heads, seq, dim).half() for _ in range(3))
+
+
+def _sdpa_cost(batch, heads, seq, dim):
+    return 4.0 * batch * heads * seq * seq * dim, 2.0 * 4 * batch * heads * seq * dim
+
+
+_add(_w("sdpa", 97, dict(batch=8, heads=16, seq=512, dim=1024), 18, _mk_sdpa,
+        _sdpa_cost(8, 16, 512, 1024), "tensor"))
+
+
 def cost_for(name: str, **shapes) -> Tuple[float, float]:
     """(flops, min_bytes) of a workload at overridden shapes."""
     w = WORKLOADS[name]
@@ -202,5 +217,7 @@ def cost_for(name: str, **shapes) -> Tuple[float, float]:
         return float(s["m"] * s["n"]), 8.0 * s["m"] * s["n"]
     if name == "pointwise_conv":
         return _conv_cost(s["batch"], s["cin"], s["cout"], s["h"], s["w"])
+    if name == "sdpa":
+        return _sdpa_cost(s["batch"], s["heads"], s["seq"], s["dim"])
     n = s["n"]
     return _gemm_cost(n, n, n)

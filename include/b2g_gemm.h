@@ -31,6 +31,7 @@
  *   kernels/4_Matrix_vector_multiplication_best_kernel.cu:84    gemv_cuda                -> b2g_gemv
  *   kernels/5_Matrix_scalar_multiplication_best_kernel.cu:47    matrix_scalar_mult_cuda  -> b2g_scale
  *   kernels/87_conv_pointwise_2D_best_kernel.cu:451             pointwise_conv_cuda      -> b2g_pointwise_conv
+ *   kernels/97_ScaledDotProductAttention_best_kernel.cu:256     fused_attention_cuda     -> b2g_sdpa
  *
  * Error behaviour: every entry point returns a b2g_status; 0 is success.
  * Nothing traps or asserts on the device.  Kernel-side waits are bounded;
@@ -196,6 +197,19 @@ B2G_API int b2g_pointwise_conv(const float* in, const float* weight, const float
                                float* out, int64_t batch, int64_t in_channels,
                                int64_t out_channels, int64_t spatial, int precision,
                                void* workspace, int64_t workspace_bytes, b2g_stream_t stream);
+
+/*
+ * Scaled-dot-product attention, fp16 in and out, fp32 accumulation and softmax:
+ *   out[b][h] = softmax(q[b][h] . k[b][h]^T * scale) . v[b][h]
+ * q, k, v, out: dense (batch, heads, seq, dim) fp16 (IEEE binary16) arrays,
+ * 16-byte aligned; seq <= 512, dim a multiple of 64.  scale <= 0 selects
+ * 1/sqrt(dim).  One tcgen05 kernel: S = q k^T in tensor memory, the full-row
+ * softmax on chip, P (fp16) . v, output scaled by 1/rowsum.
+ * Replaces fused_attention_cuda (kernels/97_ScaledDotProductAttention_best_kernel.cu:256),
+ * which requires seq == 512 in practice and dim == 1024 (:9-10, :267-268).
+ */
+B2G_API int b2g_sdpa(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                     int64_t heads, int64_t seq, int64_t dim, float scale, b2g_stream_t stream);
 
 /* Read and clear the device-side error word of `device` (synchronises it). */
 B2G_API int b2g_read_device_error(int device, int32_t* code);

@@ -49,6 +49,7 @@ REF_FUNCS = {
     17: ("17_Matmul_with_transposed_B_best_kernel.cu", "matmul_cuda", 267),
     18: ("18_Matmul_with_transposed_both_best_kernel.cu", "matmul_transposed_cuda", 152),
     87: ("87_conv_pointwise_2D_best_kernel.cu", "pointwise_conv_cuda", 451),
+    97: ("97_ScaledDotProductAttention_best_kernel.cu", "fused_attention_cuda", 256),
 }
 
 EXT = sysconfig.get_config_var("EXT_SUFFIX")
@@ -86,6 +87,8 @@ def build_one(pid: int, verbose: bool = False, force: bool = False) -> Path:
     second = "float s" if pid == 5 else "torch::Tensor B"   # K5 takes a scalar (K5:47)
     if pid == 87:   # K87:451 takes (input, weight, optional bias)
         second = "torch::Tensor B, c10::optional<torch::Tensor> bias"
+    if pid == 97:   # K97:256 takes (Q, K, V)
+        second = "torch::Tensor B, torch::Tensor V"
     extra = ', py::arg("input"), py::arg("weight"), py::arg("bias") = py::none()' if pid == 87 else ""
     shim.write_text(
         "#include <torch/extension.h>\n"

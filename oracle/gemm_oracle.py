@@ -31,6 +31,10 @@ Operator semantics (reference file:line):
   pointwise conv: out[n,o,h,w] = sum_c W[o,c] x[n,c,h,w] + bias[o]
          (K87 accumulates over in_channels, :340, then adds the bias,
          :374-386)                                  kernels/87_...:451
+  attention: out = softmax(Q K^T / sqrt(D)) V per (batch, head), fp16 in
+         and out (K97 scales by 1/sqrt(embed_dim), :266, takes the row max,
+         exponentials and their sum, :41-89, then weights V, :205-224)
+                                                    kernels/97_...:256
 """
 from __future__ import annotations
 
@@ -117,12 +121,22 @@ def pointwise_conv(x, weight, bias=None):
     return out.reshape(n, w.shape[0], h, wd)
 
 
+def sdpa(Q, K, V):
+    """out (B, H, S, D) = softmax(Q K^T / sqrt(D)) V in float64   kernels/97_...:256"""
+    q, k, v = _f64(Q), _f64(K), _f64(V)
+    s = np.einsum("bhqd,bhkd->bhqk", q, k) / np.sqrt(q.shape[-1])
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p = p / p.sum(axis=-1, keepdims=True)
+    return np.einsum("bhqk,bhkd->bhqd", p, v)
+
+
 BY_PID = {
     4: gemv, 5: matrix_scalar,
     1: square, 2: standard, 3: batched, 6: large_k, 7: small_k, 8: irregular,
     9: tall_skinny, 10: tensor3d, 11: tensor4d, 12: diag, 13: symmetric,
     14: upper_tri, 15: lower_tri, 16: transposed_a, 17: transposed_b, 18: transposed_both,
-    87: pointwise_conv,
+    87: pointwise_conv, 97: sdpa,
 }
 
 

@@ -81,6 +81,14 @@ cases.append({"pid": 87, "name": "conv1x1_bias", "A": [[x0, x1]], "B": wt, "bias
 cases.append({"pid": 87, "name": "conv1x1_nobias", "A": [[x0, x1]], "B": wt,
               "C": [[x0, x1, [[-4.0, -4.0], [-4.0, -4.0]]]]})
 
+# Attention: identical keys give a uniform softmax, so every output row is the
+# mean of V's rows; a single key gives V itself.
+cases.append({"pid": 97, "name": "sdpa_uniform", "A": [[[[1.0, 0.0], [0.0, 1.0]]]],
+              "B": [[[[1.0, 1.0], [1.0, 1.0]]]], "V": [[[[1.0, 2.0], [3.0, 4.0]]]],
+              "C": [[[[2.0, 3.0], [2.0, 3.0]]]]})
+cases.append({"pid": 97, "name": "sdpa_one_key", "A": [[[[0.5, -2.0]]]], "B": [[[[3.0, 1.0]]]],
+              "V": [[[[-1.0, 7.0]]]], "C": [[[[-1.0, 7.0]]]]})
+
 out = Path(__file__).with_name("known_answers.json")
 out.write_text(json.dumps({"cases": cases}, indent=0))
 print(f"wrote {len(cases)} cases to {out}")

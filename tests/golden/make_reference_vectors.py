@@ -50,6 +50,10 @@ CASES = {
     # 8-wide weight loads need Cout % 128 == 0 and Cin % 8 == 0, 8-wide input
     # loads need H*W % 8 == 0, and full 64-position tiles N*H*W % 64 == 0.
     87: ([(2, 40, 4, 16), (128, 40, 1, 1), (128,)], None),
+    # K97: fp16 Q, K, V (batch, heads, seq, dim); its loops assume seq == 512
+    # and dim == 1024 (kernels/97_ScaledDotProductAttention_best_kernel.cu:9-10,
+    # :102, :182).  First 16 query rows kept.
+    97: ([(1, 1, 512, 1024)] * 3, 16),
 }
 SEED0 = 1234
 
@@ -66,6 +70,8 @@ def inputs(pid):
         ts = [torch.triu(t) for t in ts]
     if pid == 15:
         ts = [torch.tril(t) for t in ts]
+    if pid == 97:
+        ts = [t.half() for t in ts]
     return ts
 
 
@@ -81,7 +87,7 @@ def main():
         C = C.cpu().numpy()
         if keep is not None:
             C = C[..., :keep, :]                 # leading rows of every output matrix
-        out[f"p{pid}"] = C.astype(np.float32)
+        out[f"p{pid}"] = C.astype(np.float32)   # (fp16 outputs are exact in fp32)
         print(pid, C.shape, flush=True)
     np.savez_compressed(Path(__file__).with_name("reference_outputs.npz"), **out)
 

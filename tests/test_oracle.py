@@ -18,7 +18,7 @@ def _cases():
 def test_known_answers(case):
     f = O.BY_PID[case["pid"]]
     B = case["B"] if case["pid"] == 5 else np.array(case["B"], dtype=np.float32)
-    extra = [np.array(case["bias"], dtype=np.float32)] if "bias" in case else []
+    extra = [np.array(case[key], dtype=np.float32) for key in ("bias", "V") if key in case]
     got = f(np.array(case["A"], dtype=np.float32), B, *extra)
     np.testing.assert_array_equal(np.asarray(got, dtype=np.float64), np.array(case["C"]))
 

