@@ -1107,14 +1107,14 @@ extern "C" int b2g_sdpa(const void* q, const void* k, const void* v, void* out, 
   if (rc != B2G_OK) return rc;
   CUtensorMap mq, mk, mv;
   if (!make_map_f16(&mq, q, dim, seq, bh, sdpa::kBM) ||
-      !make_map_f16(&mk, k, dim, seq, bh, sdpa::kKBox) ||
+      !make_map_f16(&mk, k, dim, seq, bh, sdpa::kKBox / 2) ||
       !make_map_f16(&mv, v, dim, seq, bh, sdpa::kVKeys))
     return B2G_ERR_UNSUPPORTED;
   sdpa::Params p;
   p.S = static_cast<int>(seq);
   p.D = static_cast<int>(dim);
   p.BH = static_cast<int>(bh);
-  p.qblocks = static_cast<int>(cdiv(seq, sdpa::kBM));
+  p.qblocks = static_cast<int>(cdiv(seq, sdpa::kUnitM));
   p.units = bh * p.qblocks;
   const float sc = scale > 0.f ? scale : 1.0f / std::sqrt(static_cast<float>(dim));
   p.scale_log2 = sc * 1.4426950408889634f;
@@ -1130,8 +1130,22 @@ extern "C" int b2g_sdpa(const void* q, const void* k, const void* v, void* out, 
       return B2G_ERR_LAUNCH;
     configured_dev = dev;
   }
-  const int grid = static_cast<int>(std::min<int64_t>(p.units, ds->num_sms));
-  sdpa::sdpa_kernel<<<grid, sdpa::kThreads, sdpa::kSmemBytes, stream>>>(mq, mk, mv, p);
+  // CTA pairs (clusters of 2), persistent: one pair per two SMs at most.
+  const int pairs = static_cast<int>(std::min<int64_t>(p.units, ds->num_sms / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(sdpa::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = sdpa::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, sdpa::sdpa_kernel, mq, mk, mv, p) != cudaSuccess)
+    return B2G_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
 }
 
