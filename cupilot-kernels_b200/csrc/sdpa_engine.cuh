@@ -15,7 +15,8 @@
 //            dim, 64 wide; phase 2 streams V in 128-key slices, this CTA's
 //            half of each output chunk of up to 256 columns.
 //   warp 1   MMA issuer (the pair leader's lane 0): phase 1 accumulates
-//            S = Q K^T for all keys (<= 512) into TMEM columns [0, 512);
+//            S = Q K^T for all keys (<= 512) into TMEM columns [0, 512) from a
+//            7-slot ring (3 slots plus the P buffer, idle until the softmax);
 //            phase 2 accumulates O = P V chunk by chunk into two 256-column
 //            TMEM buffers.
 //   warps 2-9 two warps per TMEM lane quadrant, each one thread per query
@@ -42,7 +43,8 @@ constexpr int kKeysMax = 512;      // S uses all 512 TMEM columns
 constexpr int kKBox = 256;         // keys per phase-1 MMA (N); 128 of them per CTA
 constexpr int kVKeys = 128;        // keys per phase-2 stage
 constexpr int kOChunk = 256;       // output columns per TMEM buffer; 128 loaded per CTA
-constexpr int kStages = 3;
+constexpr int kStages = 3;          // stage slots outside the P buffer (phase 2 uses these)
+constexpr int kSlots1 = 7;          // phase 1 also borrows the idle P buffer: 3 + 4 slots
 constexpr int kQBytes = kBM * kBD * 2;             // 16 KB
 constexpr int kKBytes = (kKBox / 2) * kBD * 2;     // 16 KB: this CTA's 128 keys
 constexpr int kVBoxBytes = kVKeys * 64 * 2;        // 16 KB: 128 keys x 64 columns
@@ -50,7 +52,7 @@ constexpr int kStageBytes = kQBytes + kKBytes;     // 32 KB (a V stage: 2 boxes 
 constexpr int kPBlockBytes = kBM * 64 * 2;         // 16 KB: 128 rows x 64 keys
 constexpr int kOffP = kStages * kStageBytes;
 constexpr int kOffBar = kOffP + (kKeysMax / 64) * kPBlockBytes;
-constexpr int kNumBars = 2 * kStages + 7;
+constexpr int kNumBars = 2 * kSlots1 + 8;
 constexpr int kOffRed = kOffBar + kNumBars * 8;    // row partials of the two halves: 2 x 128 floats
 constexpr int kOffMisc = kOffRed + 2 * kBM * 4;
 constexpr int kSmemBytes = kOffMisc + 16 + 1024;
@@ -125,12 +127,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* full = bars;
-  uint64_t* empty = bars + kStages;
-  uint64_t* s_full = bars + 2 * kStages;
+  uint64_t* empty = bars + kSlots1;
+  uint64_t* s_full = bars + 2 * kSlots1;
   uint64_t* p_ready = s_full + 1;
   uint64_t* o_full = s_full + 2;
   uint64_t* o_empty = s_full + 4;
   uint64_t* mma_drain = s_full + 6;
+  uint64_t* p_free = s_full + 7;     // the last P . V MMA of a unit has read P
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
 
@@ -143,12 +146,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nd = p.D / kBD;                          // phase-1 dim slices
   const int nkb = (p.S + kVKeys - 1) / kVKeys;       // phase-2 key slices
   const int nchunks = (p.D + kOChunk - 1) / kOChunk;
+  const int n1 = nd * nk;                            // phase-1 stages per unit
+  // Stage i of a unit lives in slot i % 7 in phase 1 (slots 3-6 are the P
+  // buffer, free until the softmax writes P), in slot (i - n1) % 3 in phase 2.
+  auto slot_of = [&](int i) -> int { return i < n1 ? i % kSlots1 : (i - n1) % kStages; };
+  auto slot_ptr = [&](int slot) -> uint8_t* {
+    return slot < kStages ? smem + slot * kStageBytes : smem + kOffP + (slot - kStages) * kStageBytes;
+  };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kSlots1; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
+    ptx::mbar_init(p_free, 1);
     ptx::mbar_init(s_full, 1);
     ptx::mbar_init(p_ready, 2 * kRowWarps);          // both CTAs' row warps (leader's)
     for (int b = 0; b < 2; ++b) {
@@ -179,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t full_leader = ptx::mapa_shared(ptx::smem_addr(full), 0);
       // A unit's stages: nd*nk (Q slice, K keys) pairs, then nchunks*nkb V slices.
-      const int n1 = nd * nk, n_items = n1 + nchunks * nkb;
+      const int n_items = n1 + nchunks * nkb;
       // Issue the boxes of stage `i` of unit `w` into stage memory `st`.
       auto stage_boxes = [&](long long w, int i, uint8_t* st, uint32_t bar) {
         const int bh = static_cast<int>(w / p.qblocks);
@@ -202,12 +213,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c = (i - n1) / nkb;
         return static_cast<uint32_t>(chunk_width_padded(p.D, c) / 128) * kVBoxBytes;
       };
-      uint32_t it = 0;
+      uint32_t uses[kSlots1] = {0, 0, 0, 0, 0, 0, 0};
+      uint32_t unit_i = 0;
       bool ok = true;
-      for (long long w = unit0; w < p.units && ok; w += unit_step) {
+      for (long long w = unit0; w < p.units && ok; w += unit_step, ++unit_i) {
         for (int i = 0; i < n_items; ++i) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+          const int s = slot_of(i);
+          // First P-buffer slot of this unit: the previous unit's P . V is done.
+          if (i == kStages && unit_i > 0 &&
+              !ptx::mbar_wait(p_free, (unit_i - 1) & 1, abort_flag, p.wait_limit_ns)) {
+            sdpa_error(p.err, abort_flag, kErrSdpaEmpty);
+            ok = false;
+            break;
+          }
+          const uint32_t ph = uses[s]++ & 1;
           if (!ptx::mbar_wait(&empty[s], ph ^ 1, abort_flag, p.wait_limit_ns)) {
             sdpa_error(p.err, abort_flag, kErrSdpaEmpty);
             ok = false;
@@ -215,35 +234,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // The leader's barrier counts both CTAs' bytes.
           if (leader) ptx::mbar_arrive_expect_tx(&full[s], 2 * stage_bytes(i));
-          ++it;
-          stage_boxes(w, i, smem + s * kStageBytes, full_leader + s * 8);
+          stage_boxes(w, i, slot_ptr(s), full_leader + s * 8);
         }
       }
       // Drain: every issued load lands before the CTA may exit (bounded).
       // The leader's barriers count the peer's loads too.
       if (leader) {
         volatile int never = 0;
-        const uint32_t first = it > static_cast<uint32_t>(kStages) ? it - kStages : 0u;
-        for (uint32_t j = first; j < it; ++j)
-          ptx::mbar_wait(&full[j % kStages], (j / kStages) & 1, &never, kDrainLimitNs);
+        for (int s = 0; s < kSlots1; ++s)
+          if (uses[s] > 0) ptx::mbar_wait(&full[s], (uses[s] - 1) & 1, &never, kDrainLimitNs);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && leader) {
       constexpr uint32_t idesc_s = ptx::idesc_f16(kUnitM, kKBox, false, false);
-      uint32_t it = 0, unit_i = 0, qc = 0;
+      uint32_t uses[kSlots1] = {0, 0, 0, 0, 0, 0, 0};
+      uint32_t unit_i = 0, qc = 0;
       bool ok = true;
-      auto wait_full = [&](int* s_out) -> bool {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
+      auto wait_full = [&](int i, int* s_out) -> bool {
+        const int s = slot_of(i);
+        const uint32_t ph = uses[s]++ & 1;
         if (!ptx::mbar_wait(&full[s], ph, abort_flag, p.wait_limit_ns)) {
           sdpa_error(p.err, abort_flag, kErrSdpaFull);
           return false;
         }
         ptx::tc_fence_after();
         *s_out = s;
-        ++it;
         return true;
       };
       // Chunk q is the (q >> 1)-th use of O buffer q & 1: before it, the
@@ -265,8 +282,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int d = 0; d < nd && ok; ++d)
           for (int h = 0; h < nk && ok; ++h) {
             int s;
-            if (!wait_full(&s)) { ok = false; break; }
-            const uint32_t sq = ptx::smem_addr(smem + s * kStageBytes);
+            if (!wait_full(d * nk + h, &s)) { ok = false; break; }
+            const uint32_t sq = ptx::smem_addr(slot_ptr(s));
             const uint32_t sk = sq + kQBytes;
 #pragma unroll
             for (int k16 = 0; k16 < kBD / 16; ++k16) {
@@ -292,8 +309,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t d_tmem = tmem_base + (qc & 1) * kOChunk;
           for (int kb = 0; kb < nkb && ok; ++kb) {
             int s;
-            if (!wait_full(&s)) { ok = false; break; }
-            const uint32_t sv = ptx::smem_addr(smem + s * kStageBytes);
+            if (!wait_full(n1 + c * nkb + kb, &s)) { ok = false; break; }
+            const uint32_t sv = ptx::smem_addr(slot_ptr(s));
 #pragma unroll
             for (int k16 = 0; k16 < kVKeys / 16; ++k16) {
               // P: 64-key blocks of 16 KB; a 16-key step is 32 B inside a row.
@@ -311,6 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (ok) ptx::mma_commit_pair(&o_full[qc & 1], 0x3);
         }
+        if (ok) ptx::mma_commit_pair(p_free, 0x3);
       }
       // Drain: no MMA may still write TMEM when it is freed, also after an
       // early exit (bounded; immediate on the normal path).
