@@ -42,6 +42,9 @@
 #ifndef B2G_SHORTK_EPIG1
 #define B2G_SHORTK_EPIG1 4
 #endif
+#ifndef B2G_PDL
+#define B2G_PDL 1              // launch engines with programmatic stream serialization
+#endif
 #ifndef B2G_DYNAMIC_UNITS
 #define B2G_DYNAMIC_UNITS 1    // hand out work units dynamically (plain GEMMs)
 #endif
@@ -359,15 +362,24 @@ int launch_engine(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
   cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  int nattr = 0;
   if (PAIR) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[nattr].id = cudaLaunchAttributeClusterDimension;
+    attr[nattr].val.clusterDim.x = 2;
+    attr[nattr].val.clusterDim.y = 1;
+    attr[nattr].val.clusterDim.z = 1;
+    ++nattr;
   }
+  if (B2G_PDL) {
+    // Back-to-back launches: this grid's CTAs may start (and set up) on SMs
+    // the previous kernel has left; the kernel waits before touching memory.
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
   if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mad, mbd, p) != cudaSuccess)
     return B2G_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
@@ -1137,13 +1149,15 @@ extern "C" int b2g_sdpa(const void* q, const void* k, const void* v, void* out, 
   cfg.blockDim = dim3(sdpa::kThreads, 1, 1);
   cfg.dynamicSmemBytes = sdpa::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = B2G_PDL ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, sdpa::sdpa_kernel, mq, mk, mv, p) != cudaSuccess)
     return B2G_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;

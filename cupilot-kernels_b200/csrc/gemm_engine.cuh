@@ -576,6 +576,11 @@ __global__ void __launch_bounds__(
   if (PAIR) ptx::cluster_sync();   // peer barriers initialised before any remote arrive
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialization: the set-up above may
+  // overlap the previous kernel's tail; every global-memory access (operand
+  // loads, unit tables, counters, output) comes after this wait.
+  ptx::griddep_launch_dependents();
+  ptx::griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer

@@ -70,6 +70,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
 }
 
 
+// ------------------------------------------------- programmatic dependent launch
+// Let the next kernel of the stream be scheduled (its CTAs still wait in
+// griddep_wait until this grid has finished and its writes are visible).
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Wait until the grids this one depends on have completed (a no-op when the
+// kernel was launched without programmatic stream serialization).
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- clusters
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
