@@ -42,6 +42,9 @@
 #ifndef B2G_SHORTK_EPIG1
 #define B2G_SHORTK_EPIG1 4
 #endif
+#ifndef B2G_KERNEL_CLEAR
+#define B2G_KERNEL_CLEAR 1     // split-K: the first K piece clears its tile in the kernel
+#endif
 #ifndef B2G_PDL
 #define B2G_PDL 1              // launch engines with programmatic stream serialization
 #endif
@@ -146,6 +149,34 @@ unsigned long long* sched_slot() {
     base[dev].store(b);
   }
   return b + 2 * (next.fetch_add(1) % kSchedSlots);
+}
+
+// Flags of the in-kernel split-K clear (EngineParams::tile_flags): one
+// region per launch from a ring, stamped with a per-process launch epoch, so
+// stale flags never match and nothing is ever reset.  Launches sharing a
+// region are kFlagRing launches apart.
+constexpr int kFlagRing = 32;
+constexpr int kFlagTiles = 128;
+static __device__ unsigned g_tile_flags[kFlagRing][kFlagTiles * kFlagSlots];
+
+bool tile_flag_region(unsigned** region, unsigned* epoch) {
+  constexpr int kMaxDevices = 64;
+  static std::atomic<unsigned*> base[kMaxDevices];
+  static std::atomic<unsigned> next{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+  unsigned* b = base[dev].load();
+  if (!b) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_tile_flags) != cudaSuccess) return false;
+    b = static_cast<unsigned*>(addr);
+    base[dev].store(b);
+  }
+  unsigned e = next.fetch_add(1) + 1;
+  if (e == 0) e = next.fetch_add(1) + 1;     // 0 is the flags' initial value
+  *epoch = e;
+  *region = b + static_cast<size_t>(e % kFlagRing) * kFlagTiles * kFlagSlots;
+  return true;
 }
 
 // ---------------------------------------------------------------- tensor maps
@@ -850,8 +881,14 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     p.sched = sched_slot();
   }
 
-  if (p.atomic_out) {
-    // Split-K accumulates into C: clear it first.
+  // Split-K accumulates into C, which must start at zero: the first K piece
+  // of each tile clears it in the kernel (TMA stores, at most kFlagTiles
+  // tiles), else the host clears C first.
+  const int64_t n_tiles = static_cast<int64_t>(pl.tiles_m) * pl.tiles_n * d->batch;
+  if (B2G_KERNEL_CLEAR && p.atomic_out && pl.tma_store && p.tri == kTriNone &&
+      p.unit_table == nullptr && n_tiles <= kFlagTiles &&
+      tile_flag_region(&p.tile_flags, &p.epoch)) {
+  } else if (p.atomic_out) {
     for (int64_t bi = 0; bi < d->batch; ++bi) {
       cudaError_t e = cudaMemset2DAsync(d->c + bi * d->stride_c, d->ldc * 4, 0, d->n * 4, d->m,
                                         stream);

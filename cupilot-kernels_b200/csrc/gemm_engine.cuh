@@ -43,6 +43,7 @@ enum : int {
   kErrWaitTmemFull = 0x105,
   kErrWaitXform = 0x106,
   kErrWaitUnit = 0x107,
+  kErrWaitZero = 0x108,
 };
 
 struct EngineParams {
@@ -73,8 +74,17 @@ struct EngineParams {
   // last one to finish resets both to 0 for the next launch.  Only for work
   // in which every unit has at least one K block.
   unsigned long long* sched;
+  // Split-K without a host-side clear of C (TMA stores only): the K piece
+  // that starts at 0 zeroes each of its epilogue warps' chunks of the tile
+  // and then sets that warp's flag, tile_flags[tile * kFlagSlots + rank *
+  // warps + warp], to `epoch`; the other pieces' matching warps wait for the
+  // flag before their first reduce-add.  Null: C was cleared by the host.
+  unsigned* tile_flags;
+  unsigned epoch;
   int* err;
 };
+
+constexpr int kFlagSlots = 16;     // epilogue warps per tile (8 per CTA, a pair)
 
 // Depth of the per-CTA ring through which the pair leader's producer hands
 // dynamically drawn unit indices to every role of both CTAs.  A role can
@@ -913,6 +923,36 @@ __global__ void __launch_bounds__(
         }
         continue;
       }
+      unsigned* tile_flag = nullptr;
+      if (p.tile_flags != nullptr) {
+        const int tile = (u.b * p.tiles_m + u.tm) * p.tiles_n + u.tn;
+        tile_flag = p.tile_flags + tile * kFlagSlots + static_cast<int>(rank) * Cfg::kEpiWarps + ew;
+        if (u.kb_lo == 0) {
+          // First K piece: zero this warp's chunks of the tile, let the
+          // stores complete, then publish them (before waiting for the MMA).
+          if (row0 < p.M) {
+            if (lane == 0) ptx::bulk_wait_read<0>();
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<float4*>(stg + lane * 32 + j * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+            ptx::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              for (int ch = half; ch * 32 < BN && n0 + ch * 32 < p.N; ch += kParts)
+                ptx::tma_store_3d(&map_c, stg, n0 + ch * 32, row0, u.b);
+              ptx::bulk_commit();
+              ptx::bulk_wait_all();
+            }
+          }
+          __syncwarp();
+          if (lane == 0) {
+            ptx::fence_proxy_async_global();
+            __threadfence();
+            ptx::st_release_gpu(tile_flag, p.epoch);
+          }
+        }
+      }
       const int buf = tl % Cfg::kAccBufs;
       const uint32_t uph = (tl / Cfg::kAccBufs) & 1;
       if (!ptx::mbar_wait_sleepy(&tmem_full[buf], uph, abort_flag, p.wait_limit_ns)) {
@@ -920,6 +960,25 @@ __global__ void __launch_bounds__(
         break;
       }
       ptx::tc_fence_after();
+      if (tile_flag != nullptr && u.kb_lo != 0 && row0 < p.M) {
+        // Later K piece: its reduce-adds land on chunks the first piece zeroes.
+        int ok = 1;
+        if (lane == 0) {
+          const uint64_t t0 = ptx::globaltimer_ns();
+          while (ptx::ld_acquire_gpu(tile_flag) != p.epoch) {
+            if (*abort_flag || ptx::globaltimer_ns() - t0 > static_cast<uint64_t>(p.wait_limit_ns)) {
+              ok = 0;
+              break;
+            }
+            __nanosleep(64);
+          }
+          ptx::fence_proxy_async_global();
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          if (lane == 0) record_error(p.err, abort_flag, kErrWaitZero);
+          break;
+        }
+      }
       auto release = [&]() {
         ptx::tc_fence_before();
         __syncwarp();

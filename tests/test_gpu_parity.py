@@ -277,3 +277,19 @@ def test_matrix_scalar_bit_exact(ops, shape):
     A = _randn(g, *shape)
     C = ops.p5.matrix_scalar_mult_cuda(A.cuda(), 0.37)
     np.testing.assert_array_equal(C.cpu().numpy(), O.matrix_scalar(A.numpy(), 0.37))
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 65536), (1024, 2048, 4096), (300, 500, 20000)])
+def test_split_k_clears_output_in_kernel(ops, m, n, k):
+    """Split-K pieces reduce-add into C; the first piece of each tile clears it
+    in the kernel.  C starts as NaN and is written three times in a row."""
+    g = _gen(m + n + k)
+    A, B = _randn(g, 1, m, k).cuda(), _randn(g, 1, k, n).cuda()
+    C = torch.full((1, m, n), float("nan"), device="cuda")
+    ref = O.batched(A.cpu().numpy(), B.cpu().numpy())
+    for _ in range(3):
+        ops.batched_matmul_out(A, B, C)
+        torch.cuda.synchronize()
+        assert torch.isfinite(C).all()
+        _check(C, ref, "tf32")
+    assert ops.read_device_error(torch.cuda.current_device()) == 0
