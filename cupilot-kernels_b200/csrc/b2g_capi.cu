@@ -273,11 +273,32 @@ __global__ void pitch_copy_kernel(const float* __restrict__ src, float* __restri
 // kTriDiagRows-row slice of a split tile's C region set to zero (the tile's
 // K pieces then reduce-add into it).  Blocks past their y's work exit.
 constexpr int kTriDiagRows = 8;
+// The unit table and split-tile list travel as a kernel parameter (no host
+// to device copy) when they fit: `words` 16-byte words, copied by the
+// pre-pass into the workspace the engine then reads.
+constexpr int kTableParamWords = 1900;
+struct TableParam {
+  int words;       // 0: the table was copied to the workspace by the host
+  int split_off;   // word offset of the split-tile list (int2 pairs)
+  int4 w[kTableParamWords];
+};
 __global__ void __launch_bounds__(256) tri_prepare_kernel(
     const float* __restrict__ a, int64_t lda, const float* __restrict__ b, int64_t ldb, int64_t n,
     int upper, float* __restrict__ adiag, float* __restrict__ bdiag, float* __restrict__ c,
-    int64_t ldc, const int2* __restrict__ split_tiles, int n_split, int block_m, int block_n) {
+    int64_t ldc, const int2* __restrict__ split_tiles, int n_split, int block_m, int block_n,
+    int4* __restrict__ table_dst, const __grid_constant__ TableParam tp) {
   constexpr int kSlices = kTriDiagBlock / kTriDiagRows;
+  // Launched with programmatic stream serialization: let the engine launch
+  // (it waits for this grid before reading), and wait for the previous
+  // kernel, which may still read the workspace this pass rewrites.
+  ptx::griddep_launch_dependents();
+  ptx::griddep_wait();
+  if (tp.words > 0) {
+    if (blockIdx.y == 1)   // B's blocks also copy the table (grid-stride over x)
+      for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tp.words; i += gridDim.x * blockDim.x)
+        table_dst[i] = tp.w[i];
+    split_tiles = reinterpret_cast<const int2*>(tp.w + tp.split_off);
+  }
   if (blockIdx.y == 2) {
     const int slices = (block_m + kTriDiagRows - 1) / kTriDiagRows;
     if (static_cast<int>(blockIdx.x) >= n_split * slices) return;
@@ -495,6 +516,12 @@ TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int t
     l.first += items[i].weight;
     heap.push(l);
   }
+  // Within a cluster, wholly masked tiles (pure zero stores, no MMA) go
+  // first: the epilogue writes them while the first real unit's mainloop
+  // runs, instead of leaving them as a store-only tail.
+  for (auto& v : per)
+    std::stable_partition(v.begin(), v.end(),
+                          [&](int i) { return items[i].lo == items[i].hi; });
   size_t rounds = 0;
   for (const auto& v : per) rounds = std::max(rounds, v.size());
   out.units.assign(rounds * clusters, make_int4(0, 0, 0, kUnitSkip << 24));
@@ -824,17 +851,40 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     table = reinterpret_cast<int4*>(ws);
     const int2* split_list = reinterpret_cast<const int2*>(ws + round_up(tbytes, 256));
     ws += round_up(tbytes, 256) + round_up(zbytes, 256);
-    if (cudaMemcpyAsync(table, host.data(), host.size(), cudaMemcpyHostToDevice, stream) !=
-        cudaSuccess)
-      return B2G_ERR_LAUNCH;
+    // Small tables ride in the pre-pass's parameters (no copy engine, no
+    // staging of pageable memory); larger ones are copied.
+    static thread_local TableParam tparam;
+    const int64_t words = static_cast<int64_t>(host.size() + 15) / 16;
+    if (words <= kTableParamWords) {
+      host.resize(words * 16, 0);
+      tparam.words = static_cast<int>(words);
+      tparam.split_off = static_cast<int>(round_up(tbytes, 256) / 16);
+      std::memcpy(tparam.w, host.data(), host.size());
+    } else {
+      tparam.words = 0;
+      if (cudaMemcpyAsync(table, host.data(), host.size(), cudaMemcpyHostToDevice, stream) !=
+          cudaSuccess)
+        return B2G_ERR_LAUNCH;
+    }
     const int n_split = static_cast<int>(tri.split_tiles.size());
     const int64_t diag_blocks = cdiv(d->m, kTriDiagBlock) * (kTriDiagBlock / kTriDiagRows);
     const int64_t zero_blocks = static_cast<int64_t>(n_split) * cdiv(pl.block_m, kTriDiagRows);
     dim3 grid(static_cast<unsigned>(std::max(diag_blocks, zero_blocks)), n_split ? 3 : 2);
-    tri_prepare_kernel<<<grid, 256, 0, stream>>>(a, lda, b, ldb, d->m,
-                                                  d->op == B2G_OP_TRI_UPPER, adiag, bdiag, d->c,
-                                                  d->ldc, split_list, n_split, pl.block_m,
-                                                  pl.block_n);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = B2G_PDL ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, tri_prepare_kernel, a, lda, b, ldb, static_cast<int64_t>(d->m),
+                           static_cast<int>(d->op == B2G_OP_TRI_UPPER), adiag, bdiag, d->c,
+                           static_cast<int64_t>(d->ldc), split_list, n_split,
+                           static_cast<int>(pl.block_m), static_cast<int>(pl.block_n), table,
+                           tparam) != cudaSuccess)
+      return B2G_ERR_LAUNCH;
   }
 
   EngineParams p;
