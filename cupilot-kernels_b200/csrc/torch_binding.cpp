@@ -288,6 +288,26 @@ at::Tensor matrix_scalar_mult(at::Tensor A, double s) {
 // kernels/87_conv_pointwise_2D_best_kernel.cu:451 (pointwise_conv_cuda) —
 // out (N, Cout, H, W) = 1x1 convolution of input (N, Cin, H, W) with weight
 // (Cout, Cin) or (Cout, Cin, 1, 1), plus an optional per-channel bias.
+at::Tensor pointwise_conv(at::Tensor input, at::Tensor weight, c10::optional<at::Tensor> bias_opt);
+
+// The reference also dispatches fp16 and bf16 (kernels/87_...:480-481): such
+// inputs are widened to fp32, run through the same TF32 engine, and the
+// output is returned in the input's dtype.
+at::Tensor pointwise_conv_any(at::Tensor input, at::Tensor weight,
+                              c10::optional<at::Tensor> bias_opt) {
+  const auto dt = input.scalar_type();
+  if (input.is_cuda() && (dt == at::kHalf || dt == at::kBFloat16)) {
+    TORCH_CHECK(weight.scalar_type() == dt, "weight must have the input's dtype");
+    c10::optional<at::Tensor> b32;
+    if (bias_opt.has_value() && bias_opt->defined()) {
+      TORCH_CHECK(bias_opt->scalar_type() == dt, "bias must have the input's dtype");
+      b32 = bias_opt->to(at::kFloat);
+    }
+    return pointwise_conv(input.to(at::kFloat), weight.to(at::kFloat), b32).to(dt);
+  }
+  return pointwise_conv(input, weight, bias_opt);
+}
+
 at::Tensor pointwise_conv(at::Tensor input, at::Tensor weight, c10::optional<at::Tensor> bias_opt) {
   check_input(input, "input");
   check_input(weight, "weight");
@@ -395,7 +415,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv", &gemv);
   m.def("matrix_scalar_mult", &matrix_scalar_mult);
   m.def("fused_attention", &fused_attention, "softmax(Q K^T / sqrt(D)) V, fp16");
-  m.def("pointwise_conv", &pointwise_conv, "1x1 convolution, NCHW", py::arg("input"),
+  m.def("pointwise_conv", &pointwise_conv_any, "1x1 convolution, NCHW", py::arg("input"),
         py::arg("weight"), py::arg("bias") = py::none());
   m.def("gemm", &gemm, "op(A) . op(B)", py::arg("A"), py::arg("B"), py::arg("trans_a") = false,
         py::arg("trans_b") = false, py::arg("op") = 0);

@@ -124,3 +124,15 @@ def test_matches_reference_kernel(ops):
         out = ops.p87.forward(xd, wd, bd)
     err = O.rel_fro(out.double().cpu().numpy(), ref.double().cpu().numpy())
     assert err <= 1e-3, f"rel_fro vs reference kernel {err:.3e}"
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_half_and_bfloat16_inputs(ops, dtype):
+    """fp16 / bf16 in, same dtype out (as the reference's dispatch returns)."""
+    x, wt, b = _inputs(11, 2, 32, 64, 8, 8)
+    x, wt, b = x.to(dtype), wt.to(dtype), b.to(dtype)
+    out = ops.p87.forward(x.cuda(), wt.cuda(), b.cuda())
+    assert out.dtype == dtype and out.shape == (2, 64, 8, 8)
+    ref = O.pointwise_conv(x.float().numpy(), wt.float().numpy(), b.float().numpy())
+    tol = 1e-2 if dtype == torch.float16 else 2e-2   # output rounding of the narrow type
+    assert O.rel_fro(out.double().cpu().numpy(), ref) <= tol
