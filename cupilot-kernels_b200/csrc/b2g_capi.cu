@@ -304,6 +304,18 @@ __global__ void __launch_bounds__(256) tri_prepare_kernel(
     if (static_cast<int>(blockIdx.x) >= n_split * slices) return;
     const int2 t = split_tiles[blockIdx.x / slices];
     const int r0 = (blockIdx.x % slices) * kTriDiagRows;
+    const int64_t col_base = static_cast<int64_t>(t.y) * block_n;
+    if ((reinterpret_cast<uintptr_t>(c) % 16) == 0 && ldc % 4 == 0 && col_base + block_n <= n) {
+      // Whole float4s: rows of the tile are 16-byte aligned and in range.
+      for (int idx = threadIdx.x; idx < kTriDiagRows * block_n / 4; idx += blockDim.x) {
+        const int r = r0 + idx / (block_n / 4);
+        const int64_t row = static_cast<int64_t>(t.x) * block_m + r;
+        if (r < block_m && row < n)
+          *reinterpret_cast<float4*>(c + row * ldc + col_base + (idx % (block_n / 4)) * 4) =
+              make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      return;
+    }
     for (int idx = threadIdx.x; idx < kTriDiagRows * block_n; idx += blockDim.x) {
       const int r = r0 + idx / block_n;
       const int64_t row = static_cast<int64_t>(t.x) * block_m + r;
@@ -319,6 +331,21 @@ __global__ void __launch_bounds__(256) tri_prepare_kernel(
   float* dst = blockIdx.y == 0 ? adiag : bdiag;
   const int64_t base = static_cast<int64_t>(blockIdx.x / kSlices) * kTriDiagBlock;
   const int r0 = (blockIdx.x % kSlices) * kTriDiagRows;
+  if ((reinterpret_cast<uintptr_t>(src) % 16) == 0 && ld % 4 == 0 && base + kTriDiagBlock <= n) {
+    // One float4 per thread (8 rows x 128 columns = 256 float4), masked per element.
+    for (int q = threadIdx.x; q < kTriDiagRows * kTriDiagBlock / 4; q += blockDim.x) {
+      const int r = r0 + q / (kTriDiagBlock / 4), c0 = (q % (kTriDiagBlock / 4)) * 4;
+      const int64_t gi = base + r;
+      if (gi >= n) break;
+      float4 v = __ldg(reinterpret_cast<const float4*>(src + gi * ld + base + c0));
+      float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (upper ? (c0 + j < r) : (c0 + j > r)) e[j] = 0.f;
+      *reinterpret_cast<float4*>(dst + gi * kTriDiagBlock + c0) = make_float4(e[0], e[1], e[2], e[3]);
+    }
+    return;
+  }
   for (int idx = threadIdx.x; idx < kTriDiagRows * kTriDiagBlock; idx += blockDim.x) {
     const int r = r0 + idx / kTriDiagBlock, cc = idx % kTriDiagBlock;
     const int64_t gi = base + r, gc = base + cc;
