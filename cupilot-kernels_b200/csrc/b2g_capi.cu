@@ -258,8 +258,23 @@ __global__ void pitch_copy_kernel(const float* __restrict__ src, float* __restri
   for (int64_t rr = blockIdx.x; rr < total; rr += gridDim.x) {
     const int64_t b = rr / rows, r = rr - b * rows;
     const float* s = src + b * sstride + r * sld;
-    float* d = dst + b * dstride + r * dld;
-    for (int64_t c = threadIdx.x; c < dld; c += blockDim.x) d[c] = c < cols ? __ldg(s + c) : 0.f;
+    float4* d = reinterpret_cast<float4*>(dst + b * dstride + r * dld);
+    // The destination pitch is a multiple of 4 floats (16-byte rows): each
+    // thread gathers float4s from unaligned source rows, two in flight.
+    const int64_t n4 = dld / 4;
+    auto gather = [&](int64_t q) {
+      float e[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) e[j] = 4 * q + j < cols ? __ldg(s + 4 * q + j) : 0.f;
+      return make_float4(e[0], e[1], e[2], e[3]);
+    };
+    for (int64_t q = threadIdx.x; q < n4; q += 2 * blockDim.x) {
+      const int64_t q1 = q + blockDim.x;
+      const float4 v0 = gather(q);
+      const float4 v1 = q1 < n4 ? gather(q1) : make_float4(0.f, 0.f, 0.f, 0.f);
+      d[q] = v0;
+      if (q1 < n4) d[q1] = v1;
+    }
   }
 }
 
