@@ -382,10 +382,17 @@ __global__ void __launch_bounds__(256) split_lo_kernel(const float* __restrict__
   for (int64_t rr = blockIdx.x; rr < total; rr += gridDim.x) {
     const int64_t b = rr / rows, r = rr - b * rows;
     const float* s = src + b * sstride + r * sld;
-    float* d = dst + b * dstride + r * dld;
-    for (int64_t c = threadIdx.x; c < dld; c += blockDim.x) {
-      const float x = c < cols ? __ldg(s + c) : 0.f;
-      d[c] = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    float4* d = reinterpret_cast<float4*>(dst + b * dstride + r * dld);
+    // 16-byte destination rows (pitch a multiple of 4): float4 stores.
+    const int64_t n4 = dld / 4;
+    for (int64_t q = threadIdx.x; q < n4; q += blockDim.x) {
+      float e[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x = 4 * q + j < cols ? __ldg(s + 4 * q + j) : 0.f;
+        e[j] = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+      }
+      d[q] = make_float4(e[0], e[1], e[2], e[3]);
     }
   }
 }
