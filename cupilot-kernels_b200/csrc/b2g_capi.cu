@@ -25,23 +25,6 @@
 #include "gemm_engine.cuh"
 #include "sdpa_engine.cuh"
 
-// Output-bound short-K units (at most B2G_SHORTK_KB K blocks): operand
-// stages and staging boxes per epilogue warp, CTA pair / single CTA.
-#ifndef B2G_SHORTK_KB
-#define B2G_SHORTK_KB 0
-#endif
-#ifndef B2G_SHORTK_STAGES
-#define B2G_SHORTK_STAGES 3
-#endif
-#ifndef B2G_SHORTK_EPIG
-#define B2G_SHORTK_EPIG 4
-#endif
-#ifndef B2G_SHORTK_STAGES1
-#define B2G_SHORTK_STAGES1 2
-#endif
-#ifndef B2G_SHORTK_EPIG1
-#define B2G_SHORTK_EPIG1 4
-#endif
 #ifndef B2G_KERNEL_CLEAR
 #define B2G_KERNEL_CLEAR 1     // split-K: the first K piece clears its tile in the kernel
 #endif
@@ -50,9 +33,6 @@
 #endif
 #ifndef B2G_DYNAMIC_UNITS
 #define B2G_DYNAMIC_UNITS 1    // hand out work units dynamically (plain GEMMs)
-#endif
-#ifndef B2G_NONPERSIST_KB
-#define B2G_NONPERSIST_KB 0
 #endif
 #ifndef B2G_PAIR256_STAGES
 #define B2G_PAIR256_STAGES 6   // pipeline depth of the CTA-pair 256-wide engine
@@ -771,9 +751,6 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   pl->kb_per_split = static_cast<int32_t>(kbps);
   pl->work_units = tiles * splits;
   pl->grid = static_cast<int32_t>(std::min<int64_t>(pl->work_units, num_sms / ctas) * ctas);
-  if (B2G_NONPERSIST_KB > 0 && kb_total <= B2G_NONPERSIST_KB && d->op == B2G_OP_GEMM && !x3 &&
-      splits == 1)
-    pl->grid = static_cast<int32_t>(std::min<int64_t>(pl->work_units, 1 << 20) * ctas);
   pl->a_mn_major = d->trans_a ? 1 : 0;
   pl->b_mn_major = d->trans_b ? 0 : 1;
   pl->tma_store = (reinterpret_cast<uintptr_t>(d->c) % 16 == 0) && (d->ldc % 4 == 0) &&
@@ -1064,15 +1041,6 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     return launch_majors<256, 6, false, true, true>(a_mn, b_mn, maps, p, grid, stream);
   if (tri_xf)
     return launch_majors<128, 6, false, true, false>(a_mn, b_mn, maps, p, grid, stream);
-  if (B2G_SHORTK_KB > 0 && p.kb_total <= B2G_SHORTK_KB && !p.atomic_out && pl.tma_store) {
-    // Output-bound short-K units: few operand stages, a ring of staging boxes.
-    if (B2G_SHORTK_EPIG > 1 && pl.cluster_ctas == 2 && pl.block_n == 256)
-      return launch_majors<256, B2G_SHORTK_STAGES, false, false, true, B2G_SHORTK_EPIG>(
-          a_mn, b_mn, maps, p, grid, stream);
-    if (B2G_SHORTK_EPIG1 > 1 && pl.cluster_ctas == 1 && pl.block_n == 256)
-      return launch_majors<256, B2G_SHORTK_STAGES1, false, false, false, B2G_SHORTK_EPIG1>(
-          a_mn, b_mn, maps, p, grid, stream);
-  }
   if (pl.cluster_ctas == 2) {
     if (pl.block_n == 512)
       return launch_majors<512, 4, false, false, true>(a_mn, b_mn, maps, p, grid, stream);
