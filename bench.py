@@ -188,47 +188,7 @@ def adaptive_steps(fn, target_s=0.25, lo=5, hi=2000):
 
 # ---------------------------------------------------------------- workloads on device
 def device_inputs(w, seed_offset=0, **shapes):
-    """Seeded N(0,1) inputs generated directly on the device (timing only;
-    parity tests use the CPU-generated, bit-identical inputs)."""
-    g = torch.Generator(device="cuda").manual_seed(w.seed * 1000 + seed_offset)
-    s = dict(w.shapes)
-    s.update(shapes)
-    r = lambda *sh: torch.randn(*sh, generator=g, device="cuda", dtype=torch.float32)
-    n = w.name
-    if n in ("square", "small_k", "large_k", "tall_skinny", "irregular"):
-        return r(s["m"], s["k"]), r(s["k"], s["n"])
-    if n == "transposed_a":
-        return r(s["k"], s["m"]), r(s["k"], s["n"])
-    if n == "transposed_b":
-        return r(s["m"], s["k"]), r(s["n"], s["k"])
-    if n == "transposed_both":
-        return r(s["k"], s["m"]), r(s["n"], s["k"])
-    if n == "batched":
-        return r(s["batch"], s["m"], s["k"]), r(s["batch"], s["k"], s["n"])
-    if n == "tensor3d":
-        return r(s["batch"], s["m"], s["k"]), r(s["k"], s["n"])
-    if n == "tensor4d":
-        return r(s["b"], s["i"], s["j"], s["l"]), r(s["l"], s["k"])
-    if n == "diag":
-        return r(s["n"]), r(s["n"], s["n"])
-    if n == "gemv":
-        return r(s["m"], s["k"]), r(s["k"], 1)
-    if n == "matrix_scalar":
-        return r(s["m"], s["n"]), 2.5
-    if n == "upper_tri":
-        return torch.triu(r(s["n"], s["n"])), torch.triu(r(s["n"], s["n"]))
-    if n == "lower_tri":
-        return torch.tril(r(s["n"], s["n"])), torch.tril(r(s["n"], s["n"]))
-    if n == "symmetric":
-        X, Y = r(s["n"], s["n"]), r(s["n"], s["n"])
-        return (X + X.T) / 2, (Y + Y.T) / 2
-    if n == "pointwise_conv":
-        return (r(s["batch"], s["cin"], s["h"], s["w"]), r(s["cout"], s["cin"], 1, 1),
-                r(s["cout"]))
-    if n == "sdpa":
-        shape = (s["batch"], s["heads"], s["seq"], s["dim"])
-        return tuple(r(*shape).half() for _ in range(3))
-    raise KeyError(n)
+    return _pkg("workloads").device_inputs(w, seed_offset, **shapes)
 
 
 def cublas_fn(name, A, B, *rest):

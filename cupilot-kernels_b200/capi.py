@@ -66,6 +66,8 @@ def lib(path: Path | None = None) -> C.CDLL:
         h.b2g_gemm.restype = C.c_int
         h.b2g_gemm_noalloc.argtypes = [C.POINTER(GemmDesc), C.c_void_p]
         h.b2g_gemm_noalloc.restype = C.c_int
+        h.b2g_noalloc_read_error.argtypes = [C.c_int, C.POINTER(C.c_int32)]
+        h.b2g_noalloc_read_error.restype = C.c_int
         h.b2g_rowscale.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                    C.c_int64, C.c_int64, C.c_void_p]
         h.b2g_rowscale.restype = C.c_int
@@ -122,6 +124,15 @@ def gemm(desc: GemmDesc, stream: int = 0) -> int:
 def gemm_noalloc(desc: GemmDesc, stream: int = 0) -> int:
     """b2g_gemm without any device allocation (fixed 16 MiB staging scratch)."""
     return lib().b2g_gemm_noalloc(C.byref(desc), C.c_void_p(stream))
+
+
+def noalloc_read_error(device: int = 0) -> int:
+    """Read and clear b2g_gemm_noalloc's device error word (0: no wait gave up)."""
+    code = C.c_int32(0)
+    rc = lib().b2g_noalloc_read_error(device, C.byref(code))
+    if rc != B2G_OK:
+        raise RuntimeError(f"b2g_noalloc_read_error: {status_string(rc)}")
+    return code.value
 
 
 def rowscale(d, b, out, rows, cols, ldb, ldo, stream: int = 0) -> int:

@@ -16,6 +16,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <tuple>
 #include <queue>
@@ -62,6 +63,19 @@ struct DeviceState {
 std::mutex g_mu;
 DeviceState g_dev[kMaxDevices];
 
+// B2G_MAX_SMS=n (a test and tuning hook, read once per process) plans every
+// launch as if the GPU had only n SMs: a small persistent grid then walks
+// many more work units per CTA, which exercises the dynamic schedule's
+// unit ring far past its wrap at small problem sizes.
+int max_sms_override() {
+  static const int v = [] {
+    const char* e = std::getenv("B2G_MAX_SMS");
+    const int n = (e && *e) ? std::atoi(e) : 0;
+    return n >= 2 ? n : (1 << 30);
+  }();
+  return v;
+}
+
 int device_state(DeviceState** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B2G_ERR_NO_DEVICE;
@@ -71,7 +85,7 @@ int device_state(DeviceState** out) {
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return B2G_ERR_NO_DEVICE;
     if (prop.major != 10) return B2G_ERR_NO_DEVICE;
-    st.num_sms = prop.multiProcessorCount;
+    st.num_sms = std::min(prop.multiProcessorCount, max_sms_override());
     if (cudaMalloc(&st.err_word, sizeof(int)) != cudaSuccess) return B2G_ERR_LAUNCH;
     if (cudaMemset(st.err_word, 0, sizeof(int)) != cudaSuccess) return B2G_ERR_LAUNCH;
     st.init = true;
@@ -564,21 +578,26 @@ TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int t
 
 // build_tri_table memoised on everything it depends on (shape, triangle,
 // tiling, cluster count, whether K pieces may reduce-add): repeated calls of
-// one shape reuse the table instead of re-sorting it on the host.
-const TriTable& cached_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int tiles_m,
-                                 int tiles_n, int clusters, bool allow_split) {
+// one shape reuse the table instead of re-sorting it on the host.  Entries
+// are shared_ptrs: a caller keeps its table alive while another thread's
+// call evicts it from the cache.
+std::shared_ptr<const TriTable> cached_tri_table(const b2g_gemm_desc* d, int block_m,
+                                                 int block_n, int tiles_m, int tiles_n,
+                                                 int clusters, bool allow_split) {
   using Key = std::tuple<int64_t, int64_t, int, int, int, int, int, int, int>;
   static std::mutex mu;
-  static std::map<Key, TriTable> cache;
+  static std::map<Key, std::shared_ptr<const TriTable>> cache;
   const Key key{d->m, d->k, d->op, block_m, block_n, tiles_m, tiles_n, clusters, allow_split};
-  std::lock_guard<std::mutex> lk(mu);
-  auto it = cache.find(key);
-  if (it == cache.end()) {
-    if (cache.size() > 64) cache.clear();
-    it = cache.emplace(key, build_tri_table(d, block_m, block_n, tiles_m, tiles_n, clusters,
-                                            allow_split)).first;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
   }
-  return it->second;
+  auto t = std::make_shared<const TriTable>(
+      build_tri_table(d, block_m, block_n, tiles_m, tiles_n, clusters, allow_split));
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() >= 64) cache.erase(cache.begin());
+  return cache.emplace(key, std::move(t)).first->second;
 }
 
 bool valid_desc(const b2g_gemm_desc* d) {
@@ -776,19 +795,33 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   }
   if (pl->tri_diag) {
     ws += 2 * round_up(d->m * kTriDiagBlock * 4, 256);
-    const TriTable& tt = cached_tri_table(d, pl->block_m, pl->block_n, pl->tiles_m,
-                                          pl->tiles_n, pl->grid / ctas, pl->tma_store);
-    ws += round_up(static_cast<int64_t>(tt.units.size()) * sizeof(int4), 256);
-    ws += round_up(static_cast<int64_t>(tt.split_tiles.size()) * sizeof(int2), 256);
-    pl->work_units = static_cast<int64_t>(tt.units.size());
+    const auto tt = cached_tri_table(d, pl->block_m, pl->block_n, pl->tiles_m, pl->tiles_n,
+                                     pl->grid / ctas, pl->tma_store);
+    ws += round_up(static_cast<int64_t>(tt->units.size()) * sizeof(int4), 256);
+    ws += round_up(static_cast<int64_t>(tt->split_tiles.size()) * sizeof(int2), 256);
+    pl->work_units = static_cast<int64_t>(tt->units.size());
   }
   pl->workspace_bytes = ws;
   return B2G_OK;
 }
 
+// SM count the launches on the current device are planned for (no
+// allocation, no context state beyond the runtime's); 148 (a B200) when no
+// device is usable, e.g. on a build host.
+static int planning_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0) {
+    cudaGetLastError();   // clear the sticky-free error of a missing device
+    return 148;
+  }
+  return std::min(sms, max_sms_override());
+}
+
 extern "C" int64_t b2g_gemm_workspace_bytes(const b2g_gemm_desc* d) {
   b2g_gemm_plan pl;
-  if (b2g_gemm_plan_for(d, 148, &pl) != B2G_OK) return -1;
+  if (b2g_gemm_plan_for(d, planning_sms(), &pl) != B2G_OK) return -1;
   return pl.workspace_bytes;
 }
 
@@ -867,8 +900,9 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     ws += 2 * nbytes;
     // Unit table (longest-first, split long tiles) followed by the split
     // tiles' coordinates: one upload, then one pre-pass launch.
-    const TriTable& tri = cached_tri_table(d, pl.block_m, pl.block_n, pl.tiles_m, pl.tiles_n,
-                                           pl.grid / pl.cluster_ctas, pl.tma_store);
+    const auto tri_ptr = cached_tri_table(d, pl.block_m, pl.block_n, pl.tiles_m, pl.tiles_n,
+                                          pl.grid / pl.cluster_ctas, pl.tma_store);
+    const TriTable& tri = *tri_ptr;
     const int64_t tbytes = static_cast<int64_t>(tri.units.size()) * sizeof(int4);
     const int64_t zbytes = static_cast<int64_t>(tri.split_tiles.size()) * sizeof(int2);
     std::vector<char> host(round_up(tbytes, 256) + zbytes);
@@ -1303,6 +1337,7 @@ extern "C" int b2g_read_device_error(int device, int32_t* code) {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[B2G_NOALLOC_SCRATCH_BYTES];
 // Device error word of this path (bounded-wait timeouts); separate from the
 // word b2g_read_device_error reports, which b2g_gemm allocates on first use.
+// b2g_noalloc_read_error reads and clears it without allocating.
 static __device__ int g_noalloc_err;
 
 namespace {
@@ -1331,6 +1366,7 @@ int noalloc_device(NoAllocDevice** out) {
       return B2G_ERR_NO_DEVICE;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return B2G_ERR_NO_DEVICE;
+    sms = std::min(sms, max_sms_override());
     void* scratch = nullptr;
     void* err = nullptr;
     if (cudaGetSymbolAddress(&scratch, g_noalloc_scratch) != cudaSuccess) return B2G_ERR_LAUNCH;
@@ -1357,4 +1393,24 @@ extern "C" int b2g_gemm_noalloc(const b2g_gemm_desc* d, b2g_stream_t stream_hand
   if (rc != B2G_OK) return rc;
   if (pl.workspace_bytes > B2G_NOALLOC_SCRATCH_BYTES) return B2G_ERR_SCRATCH_LIMIT;
   return run_planned(d, pl, st->scratch, st->err, static_cast<cudaStream_t>(stream_handle));
+}
+
+extern "C" int b2g_noalloc_read_error(int device, int32_t* code) {
+  if (!code || device < 0 || device >= kMaxDevices) return B2G_ERR_INVALID_ARG;
+  *code = 0;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return B2G_ERR_NO_DEVICE;
+  if (cudaSetDevice(device) != cudaSuccess) return B2G_ERR_NO_DEVICE;
+  // Both copies go through the symbol (no allocation): wait for the device's
+  // work, read the word, then clear it for the next call.
+  int rc = B2G_OK;
+  int v = 0;
+  const int zero = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpyFromSymbol(&v, g_noalloc_err, sizeof(int)) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(int)) != cudaSuccess)
+    rc = B2G_ERR_LAUNCH;
+  *code = v;
+  cudaSetDevice(prev);
+  return rc;
 }

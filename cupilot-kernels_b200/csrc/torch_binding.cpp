@@ -18,7 +18,14 @@
 
 namespace {
 
+// Precision mode: a process-wide default (set_precision) and a per-thread
+// override (set_thread_precision, used by the Python `precision()` context
+// manager), so a scoped mode in one thread never changes another thread's
+// calls.
 std::atomic<int> g_precision{B2G_PREC_TF32};
+thread_local int t_precision = -1;   // -1: no override, use the default
+
+int precision_now() { return t_precision >= 0 ? t_precision : g_precision.load(); }
 
 void check_status(int rc, const char* what) {
   TORCH_CHECK(rc == B2G_OK, what, ": ", b2g_status_string(rc), " (status ", rc, ")");
@@ -91,7 +98,7 @@ at::Tensor matmul_2d(const at::Tensor& A, const at::Tensor& B, int op) {
   Operand a = as_operand(A), b = as_operand(B);
   b2g_gemm_desc d{};
   d.op = op;
-  d.precision = g_precision.load();
+  d.precision = precision_now();
   d.m = M;
   d.n = N;
   d.k = K;
@@ -182,7 +189,7 @@ void batched_matmul_into(const at::Tensor& A, const at::Tensor& B, at::Tensor& C
   TORCH_CHECK(bs <= 65535, "batch too large");
   b2g_gemm_desc d{};
   d.op = B2G_OP_GEMM;
-  d.precision = g_precision.load();
+  d.precision = precision_now();
   d.m = M;
   d.n = N;
   d.k = K;
@@ -334,7 +341,7 @@ at::Tensor pointwise_conv(at::Tensor input, at::Tensor weight, c10::optional<at:
   at::Tensor x = input.contiguous();
   at::Tensor wt = weight.contiguous();
   const float* bp = bias.defined() ? bias.data_ptr<float>() : nullptr;
-  const int prec = g_precision.load();
+  const int prec = precision_now();
   const int64_t ws = b2g_pointwise_conv_workspace_bytes(x.data_ptr<float>(), wt.data_ptr<float>(),
                                                         out.data_ptr<float>(), bs, cin, cout,
                                                         h * w, prec);
@@ -383,7 +390,15 @@ void set_precision(int64_t p) {
   TORCH_CHECK(p == B2G_PREC_TF32 || p == B2G_PREC_3XTF32, "precision must be 0 (tf32) or 1 (3xtf32)");
   g_precision.store(static_cast<int>(p));
 }
-int64_t get_precision() { return g_precision.load(); }
+int64_t get_precision() { return precision_now(); }
+int64_t get_default_precision() { return g_precision.load(); }
+// p = -1 removes this thread's override.
+void set_thread_precision(int64_t p) {
+  TORCH_CHECK(p == -1 || p == B2G_PREC_TF32 || p == B2G_PREC_3XTF32,
+              "precision must be -1 (none), 0 (tf32) or 1 (3xtf32)");
+  t_precision = static_cast<int>(p);
+}
+int64_t get_thread_precision() { return t_precision; }
 
 int64_t read_device_error(int64_t device) {
   int32_t code = 0;
@@ -420,6 +435,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "op(A) . op(B)", py::arg("A"), py::arg("B"), py::arg("trans_a") = false,
         py::arg("trans_b") = false, py::arg("op") = 0);
   m.def("set_precision", &set_precision);
-  m.def("get_precision", &get_precision);
+  m.def("get_precision", &get_precision, "the mode this thread's calls use");
+  m.def("get_default_precision", &get_default_precision);
+  m.def("set_thread_precision", &set_thread_precision);
+  m.def("get_thread_precision", &get_thread_precision);
   m.def("read_device_error", &read_device_error);
 }

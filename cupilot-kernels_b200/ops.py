@@ -31,25 +31,31 @@ PRECISIONS = {"tf32": 0, "3xtf32": 1}
 
 
 def set_precision(mode: str) -> None:
-    """Select 'tf32' (one TF32 product) or '3xtf32' (split, ~fp32 accuracy)."""
+    """Select the process-wide default: 'tf32' (one TF32 product) or
+    '3xtf32' (split, ~fp32 accuracy).  Threads inside a `precision()` block
+    keep their own mode."""
     if mode not in PRECISIONS:
         raise ValueError(f"precision must be one of {sorted(PRECISIONS)}, got {mode!r}")
     _ext.set_precision(PRECISIONS[mode])
 
 
 def get_precision() -> str:
+    """The mode this thread's calls use (its override, else the default)."""
     v = _ext.get_precision()
     return next(k for k, i in PRECISIONS.items() if i == v)
 
 
 @contextlib.contextmanager
 def precision(mode: str):
-    prev = get_precision()
-    set_precision(mode)
+    """Run the block's calls in `mode`, in this thread only."""
+    if mode not in PRECISIONS:
+        raise ValueError(f"precision must be one of {sorted(PRECISIONS)}, got {mode!r}")
+    prev = _ext.get_thread_precision()
+    _ext.set_thread_precision(PRECISIONS[mode])
     try:
         yield
     finally:
-        set_precision(prev)
+        _ext.set_thread_precision(prev)
 
 
 if os.environ.get("B2G_PRECISION"):

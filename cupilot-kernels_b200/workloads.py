@@ -221,3 +221,52 @@ def cost_for(name: str, **shapes) -> Tuple[float, float]:
         return _sdpa_cost(s["batch"], s["heads"], s["seq"], s["dim"])
     n = s["n"]
     return _gemm_cost(n, n, n)
+
+
+def device_inputs(w: Workload, seed_offset: int = 0, device="cuda", **override):
+    """Seeded N(0,1) inputs of a workload drawn directly on the device.
+
+    Large configs (GBs of operands) are generated where they are used; the
+    values differ from `Workload.inputs` (a CPU generator) but follow the
+    same recipe per config (opposite triangle zeroed, symmetric =
+    (X + X^T) / 2, attention in fp16).
+    """
+    g = torch.Generator(device=device).manual_seed(w.seed * 1000 + seed_offset)
+    s = dict(w.shapes)
+    s.update(override)
+    r = lambda *sh: torch.randn(*sh, generator=g, device=device, dtype=torch.float32)
+    n = w.name
+    if n in ("square", "small_k", "large_k", "tall_skinny", "irregular"):
+        return r(s["m"], s["k"]), r(s["k"], s["n"])
+    if n == "transposed_a":
+        return r(s["k"], s["m"]), r(s["k"], s["n"])
+    if n == "transposed_b":
+        return r(s["m"], s["k"]), r(s["n"], s["k"])
+    if n == "transposed_both":
+        return r(s["k"], s["m"]), r(s["n"], s["k"])
+    if n == "batched":
+        return r(s["batch"], s["m"], s["k"]), r(s["batch"], s["k"], s["n"])
+    if n == "tensor3d":
+        return r(s["batch"], s["m"], s["k"]), r(s["k"], s["n"])
+    if n == "tensor4d":
+        return r(s["b"], s["i"], s["j"], s["l"]), r(s["l"], s["k"])
+    if n == "diag":
+        return r(s["n"]), r(s["n"], s["n"])
+    if n == "gemv":
+        return r(s["m"], s["k"]), r(s["k"], 1)
+    if n == "matrix_scalar":
+        return r(s["m"], s["n"]), 2.5
+    if n == "upper_tri":
+        return torch.triu(r(s["n"], s["n"])), torch.triu(r(s["n"], s["n"]))
+    if n == "lower_tri":
+        return torch.tril(r(s["n"], s["n"])), torch.tril(r(s["n"], s["n"]))
+    if n == "symmetric":
+        X, Y = r(s["n"], s["n"]), r(s["n"], s["n"])
+        return (X + X.T) / 2, (Y + Y.T) / 2
+    if n == "pointwise_conv":
+        return (r(s["batch"], s["cin"], s["h"], s["w"]), r(s["cout"], s["cin"], 1, 1),
+                r(s["cout"]))
+    if n == "sdpa":
+        shape = (s["batch"], s["heads"], s["seq"], s["dim"])
+        return tuple(r(*shape).half() for _ in range(3))
+    raise KeyError(n)

@@ -121,7 +121,8 @@ typedef struct b2g_gemm_plan {
 /* Compute the plan for desc on a GPU with num_sms SMs (no device access). */
 B2G_API int b2g_gemm_plan_for(const b2g_gemm_desc* desc, int num_sms, b2g_gemm_plan* plan);
 
-/* Workspace the caller must provide for desc (0 for aligned layouts). */
+/* Workspace the caller must provide for desc (0 for aligned TF32 GEMMs),
+ * planned for the current device's SM count (148 when no device is usable). */
 B2G_API int64_t b2g_gemm_workspace_bytes(const b2g_gemm_desc* desc);
 
 /* Launch the GEMM on stream (asynchronous; no host synchronisation). */
@@ -146,22 +147,38 @@ B2G_API int b2g_rowscale(const float* d, const float* b, float* out, int64_t row
  * allocating call.
  *
  * Same descriptor and result as b2g_gemm; desc->workspace is ignored.
- * Operands whose pitch needs a 16-byte-aligned staged copy are staged in a
- * fixed file-scope device array of B2G_NOALLOC_SCRATCH_BYTES (16 MiB), which
- * every GPU that loads the library holds until the process exits.  A
- * descriptor needing more staging than that returns B2G_ERR_SCRATCH_LIMIT
- * before any work is issued (b2g_gemm_workspace_bytes() tells how much it
- * needs; aligned operands need none).
+ * Everything b2g_gemm would place in caller workspace goes into one fixed
+ * file-scope device array of B2G_NOALLOC_SCRATCH_BYTES (16 MiB), which every
+ * GPU that loads the library holds until the process exits:
+ *   - staged copies of operands whose pitch or base is not 16-byte aligned;
+ *   - every 3xTF32 call on a plain GEMM, aligned or not: the lo parts of A
+ *     and B (m*k + k*n floats per batch entry, rounded up to 16-byte rows),
+ *     so 3xTF32 fits only while A and B together hold at most ~4 M elements;
+ *   - every triangular call in TF32 on untransposed operands, aligned or
+ *     not: masked copies of the diagonal blocks (2 * n * 128 floats) and the
+ *     unit table (16 bytes per unit), so n is limited to about 16000.
+ * A descriptor needing more than that returns B2G_ERR_SCRATCH_LIMIT before
+ * any work is issued; b2g_gemm_workspace_bytes() tells how much it needs.
  *
  * The first call on a device, with that device current, looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before
  * any stream capture begins.  All calls on a device share the one array and
  * it keeps the last call's contents: calls whose work may overlap on the GPU
  * (unordered streams) race on it.  Bounded-wait timeouts in this path are
- * recorded in a word of its own, which b2g_read_device_error does not read.
+ * recorded in a device word of its own: read and clear it with
+ * b2g_noalloc_read_error(), which allocates nothing either
+ * (b2g_read_device_error does not see it).
  */
 #define B2G_NOALLOC_SCRATCH_BYTES (16ll << 20)
 B2G_API int b2g_gemm_noalloc(const b2g_gemm_desc* desc, b2g_stream_t stream);
+
+/*
+ * Read and clear the device error word of b2g_gemm_noalloc on `device`
+ * (synchronises the device; no allocation).  0: no bounded wait gave up
+ * since the last read; otherwise the code of the first wait that did (its
+ * call's output is incomplete).  No counterpart in the reference.
+ */
+B2G_API int b2g_noalloc_read_error(int device, int32_t* code);
 
 /*
  * y[i] = sum_k A[i][k] x[k]  (fp32 CUDA-core dot products, 16-byte streaming loads).
