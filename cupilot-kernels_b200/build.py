@@ -29,8 +29,9 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIB = PKG / "libb2g_sm100.so"
 EXT = PKG / ("_b2g_torch" + sysconfig.get_config_var("EXT_SUFFIX"))
 
-CU_SOURCES = [CSRC / "b2g_capi.cu", CSRC / "b2g_vector.cu"]
+CU_SOURCES = [CSRC / "b2g_capi.cu", CSRC / "b2g_vector.cu", CSRC / "b2g_peer.cu"]
 CU_DEPS = CU_SOURCES + [CSRC / "gemm_engine.cuh", CSRC / "sdpa_engine.cuh", CSRC / "ptx_sm100.cuh",
+                        CSRC / "b2g_internal.h",
                         INCLUDE / "b2g_gemm.h"]
 EXT_SOURCES = [CSRC / "torch_binding.cpp"]
 

@@ -37,6 +37,13 @@ class GemmDesc(C.Structure):
     ]
 
 
+class IpcHandle(C.Structure):
+    _fields_ = [("bytes", C.c_ubyte * 64)]
+
+
+PEER_MAX_RANKS = 16
+
+
 class GemmPlan(C.Structure):
     _fields_ = [
         ("block_m", C.c_int32), ("block_n", C.c_int32), ("block_k", C.c_int32),
@@ -84,6 +91,21 @@ def lib(path: Path | None = None) -> C.CDLL:
                                          C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int,
                                          C.c_void_p, C.c_int64, C.c_void_p]
         h.b2g_pointwise_conv.restype = C.c_int
+        h.b2g_peer_mailbox_bytes.argtypes = [C.c_int64, C.c_int]
+        h.b2g_peer_mailbox_bytes.restype = C.c_int64
+        h.b2g_peer_mailbox_create.argtypes = [C.c_int64, C.c_int, C.POINTER(C.c_void_p),
+                                              C.POINTER(IpcHandle)]
+        h.b2g_peer_mailbox_create.restype = C.c_int
+        h.b2g_peer_mailbox_open.argtypes = [C.POINTER(IpcHandle), C.POINTER(C.c_void_p)]
+        h.b2g_peer_mailbox_open.restype = C.c_int
+        h.b2g_peer_mailbox_close.argtypes = [C.c_void_p]
+        h.b2g_peer_mailbox_close.restype = C.c_int
+        h.b2g_peer_mailbox_destroy.argtypes = [C.c_void_p]
+        h.b2g_peer_mailbox_destroy.restype = C.c_int
+        h.b2g_splitk_peer_reduce.argtypes = [C.c_void_p, C.c_void_p, C.c_int64,
+                                             C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_int,
+                                             C.c_int64, C.c_void_p]
+        h.b2g_splitk_peer_reduce.restype = C.c_int
         h.b2g_read_device_error.argtypes = [C.c_int, C.POINTER(C.c_int32)]
         h.b2g_read_device_error.restype = C.c_int
         h.b2g_status_string.argtypes = [C.c_int]
@@ -150,6 +172,46 @@ def pointwise_conv(inp, weight, bias, out, batch, cin, cout, spatial, precision=
     """out[n] = weight . in[n] (+ bias per output channel), NCHW with H*W = spatial."""
     return lib().b2g_pointwise_conv(inp, weight, bias, out, batch, cin, cout, spatial, precision,
                                     workspace, workspace_bytes, C.c_void_p(stream))
+
+
+def _check(rc, what):
+    if rc != B2G_OK:
+        raise RuntimeError(f"{what}: {status_string(rc)} ({rc})")
+
+
+def peer_mailbox_bytes(elems: int, world: int) -> int:
+    return lib().b2g_peer_mailbox_bytes(elems, world)
+
+
+def peer_mailbox_create(elems: int, world: int):
+    """Create this rank's mailbox on the current device: (pointer, handle bytes)."""
+    ptr, h = C.c_void_p(), IpcHandle()
+    _check(lib().b2g_peer_mailbox_create(elems, world, C.byref(ptr), C.byref(h)),
+           "b2g_peer_mailbox_create")
+    return ptr.value, bytes(h.bytes)
+
+
+def peer_mailbox_open(handle: bytes) -> int:
+    h = IpcHandle()
+    C.memmove(h.bytes, handle, 64)
+    ptr = C.c_void_p()
+    _check(lib().b2g_peer_mailbox_open(C.byref(h), C.byref(ptr)), "b2g_peer_mailbox_open")
+    return ptr.value
+
+
+def peer_mailbox_close(ptr: int) -> None:
+    _check(lib().b2g_peer_mailbox_close(ptr), "b2g_peer_mailbox_close")
+
+
+def peer_mailbox_destroy(ptr: int) -> None:
+    _check(lib().b2g_peer_mailbox_destroy(ptr), "b2g_peer_mailbox_destroy")
+
+
+def splitk_peer_reduce(partial: int, out: int, elems: int, mailboxes, rank: int, root: int,
+                       epoch: int, stream: int = 0) -> int:
+    arr = (C.c_void_p * len(mailboxes))(*mailboxes)
+    return lib().b2g_splitk_peer_reduce(partial, out, elems, arr, len(mailboxes), rank, root,
+                                        epoch, C.c_void_p(stream))
 
 
 def read_device_error(device: int = 0) -> int:

@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "../../include/b2g_gemm.h"
+#include "b2g_internal.h"
 #include "gemm_engine.cuh"
 #include "sdpa_engine.cuh"
 
@@ -646,6 +647,15 @@ Stage stage_geom(int64_t rows, int64_t cols, int64_t nbatch, int64_t align = 4) 
 }
 
 }  // namespace
+}  // namespace b2g
+
+namespace b2g {
+int* current_error_word() {
+  DeviceState* ds = nullptr;
+  return device_state(&ds) == B2G_OK ? ds->err_word : nullptr;
+}
+long long current_wait_limit_ns() { return wait_limit_ns(); }
+bool pdl_enabled() { return B2G_PDL != 0; }
 }  // namespace b2g
 
 using namespace b2g;

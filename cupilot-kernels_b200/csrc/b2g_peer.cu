@@ -1,0 +1,277 @@
+// b2g_peer.cu — the cross-GPU step of a K split over the GPUs of one node.
+//
+// The reference's large-K kernel splits K over 8 CUDA streams on one GPU
+// and sums the partial products with 7 `C.add_` calls
+// (kernels/6_Matmul_with_large_K_dimension_best_kernel.cu:147-200).  Here K
+// is split over ranks, one process per GPU; each rank computes its partial
+// product with the GEMM engine, and the partials are summed on the root
+// over NVLink by the two kernels below, through peer memory:
+//
+//   non-root rank r: peer_push_kernel copies its partial, chunk by chunk,
+//     into landing slot [epoch % 2][r] of the root's mailbox with plain
+//     16-byte stores through the peer mapping, then stamps the chunk's
+//     ready flag ready[c][r] = epoch in the root's mailbox (release, system
+//     scope).  Before writing a chunk it waits until the root has consumed
+//     the same slot two epochs ago (consumed[c] in its own mailbox).
+//   root: peer_reduce_kernel waits for ready[c][r] >= epoch from every other
+//     rank, adds the landed chunks to its own partial (already in C, in rank
+//     order, so the sum is deterministic), and stamps consumed[c] = epoch in
+//     every other rank's mailbox.
+//
+// Every wait is bounded (B2G_WAIT_LIMIT_MS): a wait that gives up records a
+// code in the device error word and the CTA returns; nothing traps.  Only
+// plain loads and stores touch peer memory (no TMA, no bulk copies, no
+// multicast), and only the mailboxes do: the GEMM engine never sees a peer
+// pointer.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/b2g_gemm.h"
+#include "b2g_internal.h"
+#include "ptx_sm100.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int64_t kChunk = kThreads * 4;   // floats per chunk: one float4 per thread
+constexpr int kMaxRanks = B2G_PEER_MAX_RANKS;
+
+enum : int { kErrPeerCredit = 0x201, kErrPeerReady = 0x202 };
+
+inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
+
+// Mailbox layout for `elems` floats and `world` ranks:
+//   [0, flag_bytes)   ready[nchunk][world] u64, then consumed[nchunk] u64
+//   [flag_bytes, ..)  landing[2][world][elems] floats (read on the root only)
+struct Layout {
+  int64_t nchunk, ready_off, consumed_off, flag_bytes, landing_off, slot_stride, total;
+};
+Layout layout(int64_t elems, int world) {
+  Layout l;
+  l.nchunk = cdiv(elems, kChunk);
+  l.ready_off = 0;
+  l.consumed_off = l.nchunk * world * 8;
+  l.flag_bytes = round_up(l.consumed_off + l.nchunk * 8, 256);
+  l.landing_off = l.flag_bytes;
+  l.slot_stride = round_up(elems * 4, 256);             // bytes per (slot, rank) region
+  l.total = l.landing_off + 2 * world * l.slot_stride;
+  return l;
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Spin (with a short sleep) until *flag >= want; false after limit_ns.
+__device__ __forceinline__ bool wait_at_least(const uint64_t* flag, uint64_t want,
+                                              long long limit_ns) {
+  if (ld_acquire_sys(flag) >= want) return true;
+  const uint64_t t0 = b2g::ptx::globaltimer_ns();
+  while (ld_acquire_sys(flag) < want) {
+    if (b2g::ptx::globaltimer_ns() - t0 > static_cast<uint64_t>(limit_ns)) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
+struct PeerArgs {
+  unsigned char* mbox[kMaxRanks];   // every rank's mailbox as mapped in this process
+};
+
+// One CTA per chunk.  partial: this rank's partial product (elems floats).
+__global__ void __launch_bounds__(kThreads) peer_push_kernel(const float* __restrict__ partial,
+                                                             int64_t elems, PeerArgs args,
+                                                             Layout lay, int world, int rank,
+                                                             int root, long long epoch,
+                                                             long long limit_ns, int* err) {
+  // The partial was written by the preceding GEMM (programmatic launch).
+  b2g::ptx::griddep_wait();
+  __shared__ int abort_flag;
+  const int64_t c = blockIdx.x;
+  unsigned char* mine = args.mbox[rank];
+  unsigned char* rootb = args.mbox[root];
+  if (threadIdx.x == 0) {
+    // The slot this epoch writes was last read by the root two epochs ago.
+    const uint64_t* consumed = reinterpret_cast<const uint64_t*>(mine + lay.consumed_off) + c;
+    const long long need = epoch - 2;
+    abort_flag = (need > 0 && !wait_at_least(consumed, static_cast<uint64_t>(need), limit_ns));
+    if (abort_flag && err) atomicCAS(err, 0, kErrPeerCredit);
+  }
+  __syncthreads();
+  if (abort_flag) return;
+  float* dst = reinterpret_cast<float*>(rootb + lay.landing_off +
+                                        ((epoch & 1) * world + rank) * lay.slot_stride);
+  const int64_t i = c * kChunk + static_cast<int64_t>(threadIdx.x) * 4;
+  if (i + 4 <= elems) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(partial + i));
+    *reinterpret_cast<float4*>(dst + i) = v;
+  } else {
+    for (int64_t j = i; j < elems; ++j) dst[j] = __ldcg(partial + j);
+  }
+  // Every thread's peer stores are ordered before the flag.
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t* ready = reinterpret_cast<uint64_t*>(rootb + lay.ready_off) + c * world + rank;
+    st_release_sys(ready, static_cast<uint64_t>(epoch));
+  }
+}
+
+// Root, one CTA per chunk: out += sum over the other ranks of their landed
+// partials, in rank order.
+__global__ void __launch_bounds__(kThreads) peer_reduce_kernel(float* __restrict__ out,
+                                                               int64_t elems, PeerArgs args,
+                                                               Layout lay, int world, int root,
+                                                               long long epoch, long long limit_ns,
+                                                               int* err) {
+  // out holds this rank's own partial, written by the preceding GEMM.
+  b2g::ptx::griddep_wait();
+  __shared__ int abort_flag;
+  const int64_t c = blockIdx.x;
+  unsigned char* mine = args.mbox[root];
+  if (threadIdx.x == 0) abort_flag = 0;
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < world && t != root) {
+    const uint64_t* ready = reinterpret_cast<const uint64_t*>(mine + lay.ready_off) + c * world + t;
+    if (!wait_at_least(ready, static_cast<uint64_t>(epoch), limit_ns)) {
+      atomicExch(&abort_flag, 1);
+      if (err) atomicCAS(err, 0, kErrPeerReady);
+    }
+  }
+  __syncthreads();
+  if (abort_flag) return;
+  const float* slot = reinterpret_cast<const float*>(mine + lay.landing_off +
+                                                     (epoch & 1) * world * lay.slot_stride);
+  const int64_t stride = lay.slot_stride / 4;
+  const int64_t i = c * kChunk + static_cast<int64_t>(t) * 4;
+  if (i + 4 <= elems) {
+    float4 acc = *reinterpret_cast<const float4*>(out + i);
+    for (int r = 0; r < world; ++r) {
+      if (r == root) continue;
+      // L2 loads: the landed data was written by another GPU since this
+      // SM may last have cached the slot.
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(slot + r * stride + i));
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    *reinterpret_cast<float4*>(out + i) = acc;
+  } else {
+    for (int64_t j = i; j < elems; ++j) {
+      float acc = out[j];
+      for (int r = 0; r < world; ++r)
+        if (r != root) acc += __ldcg(slot + r * stride + j);
+      out[j] = acc;
+    }
+  }
+  __syncthreads();   // every thread's reads of the slot are done
+  if (t < world && t != root) {
+    uint64_t* consumed = reinterpret_cast<uint64_t*>(args.mbox[t] + lay.consumed_off) + c;
+    st_release_sys(consumed, static_cast<uint64_t>(epoch));
+  }
+}
+
+}  // namespace
+
+extern "C" int64_t b2g_peer_mailbox_bytes(int64_t elems, int world) {
+  if (elems <= 0 || world < 1 || world > kMaxRanks) return -1;
+  return layout(elems, world).total;
+}
+
+extern "C" int b2g_peer_mailbox_create(int64_t elems, int world, void** mailbox,
+                                       b2g_ipc_handle* handle) {
+  if (!mailbox || !handle || elems <= 0 || world < 1 || world > kMaxRanks)
+    return B2G_ERR_INVALID_ARG;
+  *mailbox = nullptr;
+  const Layout l = layout(elems, world);
+  void* p = nullptr;
+  if (cudaMalloc(&p, l.total) != cudaSuccess) return B2G_ERR_LAUNCH;
+  // Flags start at 0 (no epoch yet); landing slots need no initial value.
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, l.flag_bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return B2G_ERR_LAUNCH;
+  }
+  static_assert(sizeof(h) <= sizeof(handle->bytes), "IPC handle does not fit");
+  std::memset(handle->bytes, 0, sizeof(handle->bytes));
+  std::memcpy(handle->bytes, &h, sizeof(h));
+  *mailbox = p;
+  return B2G_OK;
+}
+
+extern "C" int b2g_peer_mailbox_open(const b2g_ipc_handle* handle, void** mailbox) {
+  if (!handle || !mailbox) return B2G_ERR_INVALID_ARG;
+  *mailbox = nullptr;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+    return B2G_ERR_LAUNCH;
+  *mailbox = p;
+  return B2G_OK;
+}
+
+extern "C" int b2g_peer_mailbox_close(void* mailbox) {
+  if (!mailbox) return B2G_ERR_INVALID_ARG;
+  return cudaIpcCloseMemHandle(mailbox) == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
+}
+
+extern "C" int b2g_peer_mailbox_destroy(void* mailbox) {
+  if (!mailbox) return B2G_ERR_INVALID_ARG;
+  return cudaFree(mailbox) == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
+}
+
+extern "C" int b2g_splitk_peer_reduce(const float* partial, float* out, int64_t elems,
+                                      void* const* mailboxes, int world, int rank, int root,
+                                      int64_t epoch, b2g_stream_t stream_handle) {
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || root < 0 || root >= world)
+    return B2G_ERR_INVALID_ARG;
+  if (elems < 0 || epoch < 1 || !mailboxes) return B2G_ERR_INVALID_ARG;
+  if (elems == 0 || world == 1) return B2G_OK;
+  const bool is_root = rank == root;
+  if (is_root ? !out : !partial) return B2G_ERR_INVALID_ARG;
+  const void* mine = is_root ? static_cast<const void*>(out) : static_cast<const void*>(partial);
+  if (reinterpret_cast<uintptr_t>(mine) % 16) return B2G_ERR_UNSUPPORTED;
+  PeerArgs args;
+  std::memset(&args, 0, sizeof(args));
+  for (int r = 0; r < world; ++r) {
+    if (!mailboxes[r]) return B2G_ERR_INVALID_ARG;
+    args.mbox[r] = static_cast<unsigned char*>(mailboxes[r]);
+  }
+  int* err = b2g::current_error_word();
+  if (!err) return B2G_ERR_NO_DEVICE;
+  const Layout lay = layout(elems, world);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(lay.nchunk), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.stream = stream;
+  // Programmatic launch after the GEMM that produced the partial: the set-up
+  // overlaps the GEMM's tail; the kernels wait for it before reading.
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = b2g::pdl_enabled() ? 1 : 0;
+  const long long limit = b2g::current_wait_limit_ns();
+  cudaError_t e;
+  if (is_root)
+    e = cudaLaunchKernelEx(&cfg, peer_reduce_kernel, out, elems, args, lay, world, root,
+                           static_cast<long long>(epoch), limit, err);
+  else
+    e = cudaLaunchKernelEx(&cfg, peer_push_kernel, partial, elems, args, lay, world, rank, root,
+                           static_cast<long long>(epoch), limit, err);
+  if (e != cudaSuccess) return B2G_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? B2G_OK : B2G_ERR_LAUNCH;
+}

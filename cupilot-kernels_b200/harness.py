@@ -88,13 +88,13 @@ def model_ref(pid: int) -> ModelRef:
 def pids():
     """Problem IDs with both a module and a benchmark workload."""
     have = {w.pid for w in workloads.WORKLOADS.values()}
-    return sorted(p for p in have if p in (1, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17,
+    return sorted(p for p in have if p in (1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17,
                                             18, 87, 97))
 
 
 # Shrunk shapes for quick checks (same structure as the workload's config).
 _SMALL = {
-    "square": dict(m=256, n=256, k=256), "batched": dict(batch=4, m=128, n=256, k=128),
+    "square": dict(m=256, n=256, k=256), "standard": dict(m=256, n=384, k=512), "batched": dict(batch=4, m=128, n=256, k=128),
     "small_k": dict(m=512, n=384, k=32), "large_k": dict(m=64, n=64, k=8192),
     "tall_skinny": dict(m=512, n=512, k=64), "irregular": dict(m=205, n=121, k=149),
     "tensor3d": dict(batch=2, m=128, n=96, k=256), "tensor4d": dict(b=2, i=4, j=8, l=64, k=96),

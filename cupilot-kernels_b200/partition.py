@@ -9,8 +9,11 @@ Two ways to spread one operator call over the GPUs of a node:
 * K splitting (large-K, reference kernels/6_Matmul_with_large_K_dimension_best_kernel.cu,
   whose 8 streams + 7 `C.add_` on one GPU at K6:147-200 become ranks +
   a reduction): rank r multiplies A[:, K_r] by B[K_r, :] locally, then the
-  partial products are summed by one NCCL reduce over NVLink to the root
-  (or an all-reduce when every rank needs C).
+  partial products are summed on the root over NVLink.  On GPUs the sum
+  is the library's own peer-memory reduction (b2g_splitk_peer_reduce: each
+  rank pushes its partial into the root's mailbox right behind its GEMM, the
+  root adds them; no NCCL call, no host synchronisation); otherwise, or when
+  every rank needs C, one NCCL (gloo on CPU) reduce / all-reduce.
 
 The local product is the package's own GEMM (`ops`); callers may inject a
 different `local_matmul` (the host-side tests run the orchestration on CPU
@@ -113,20 +116,95 @@ class Partitioner:
         return k_split_plan(k, self.world)[self.rank]
 
     def split_k_matmul(self, A_k: torch.Tensor, B_k: torch.Tensor, root: int = 0,
-                       all_ranks: bool = False) -> Optional[torch.Tensor]:
+                       all_ranks: bool = False, method: str = "auto") -> Optional[torch.Tensor]:
         """Given this rank's K slice (A[:, K_r], B[K_r, :]), return C = A B on
-        the root (None elsewhere), or on every rank when all_ranks."""
+        the root (None elsewhere), or on every rank when all_ranks.
+
+        method: "peer" sums the partials with the peer-memory reduction (CUDA
+        tensors, one node), "collective" with one NCCL / gloo reduce; "auto"
+        picks "peer" for CUDA tensors on more than one rank unless all_ranks.
+        """
         if A_k.shape[1] == 0:
             part = torch.zeros(A_k.shape[0], B_k.shape[1], dtype=A_k.dtype, device=A_k.device)
         else:
             part = self._mm()(A_k, B_k)
         if self.world == 1:
             return part
+        if method == "auto":
+            method = "peer" if (A_k.is_cuda and not all_ranks) else "collective"
+        if method == "peer":
+            if all_ranks:
+                raise ValueError("the peer reduction delivers C to the root only")
+            red = self.peer_reducer(part.numel())
+            red.reduce(part, part if self.rank == root else None, root)
+            return part if self.rank == root else None
         if all_ranks:
             dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
             return part
         dist.reduce(part, dst=root, op=dist.ReduceOp.SUM, group=self.group)
         return part if self.rank == root else None
+
+    def peer_reducer(self, elems: int, backend=None) -> "PeerReducer":
+        """The mailbox set for partials of `elems` floats, created on first use
+        (a collective call: every rank must reach it)."""
+        cache = self.__dict__.setdefault("_peer", {})
+        if elems not in cache:
+            cache[elems] = PeerReducer(self, elems, backend)
+        return cache[elems]
+
+
+class PeerReducer:
+    """Mailboxes of the peer-memory K-split reduction for one partial size.
+
+    Every rank creates its mailbox (device memory, b2g_peer_mailbox_create),
+    the IPC handles are exchanged with one all_gather_object over the
+    process group, and every rank opens the others'.  `reduce` then runs one
+    epoch of the protocol on the current stream: the root adds the other
+    ranks' partials into `out` (which holds its own); the others push theirs.
+    All ranks must call `reduce` in the same order.  `backend` is the C-ABI
+    binding (capi); tests inject a stand-in.
+    """
+
+    def __init__(self, part: "Partitioner", elems: int, backend=None):
+        if backend is None:
+            import importlib
+
+            backend = importlib.import_module(__package__ + ".capi")
+        self.backend = backend
+        self.part = part
+        self.elems = int(elems)
+        self.epoch = 0
+        own, handle = backend.peer_mailbox_create(self.elems, part.world)
+        handles = [None] * part.world
+        dist.all_gather_object(handles, handle, group=part.group)
+        self.own = own
+        self.mailboxes = [own if r == part.rank else backend.peer_mailbox_open(handles[r])
+                          for r in range(part.world)]
+        # Every rank has opened every mailbox before any rank writes into one.
+        dist.barrier(group=part.group)
+
+    def reduce(self, partial: Optional[torch.Tensor], out: Optional[torch.Tensor],
+               root: int = 0) -> None:
+        """Root: out += the other ranks' partials.  Others: push `partial`."""
+        self.epoch += 1
+        is_root = self.part.rank == root
+        t = out if is_root else partial
+        if t is None or t.numel() != self.elems or not t.is_contiguous():
+            raise ValueError("peer reduce needs a contiguous tensor of the mailbox's size")
+        stream = torch.cuda.current_stream(t.device).cuda_stream if t.is_cuda else 0
+        rc = self.backend.splitk_peer_reduce(0 if is_root else t.data_ptr(),
+                                             t.data_ptr() if is_root else 0, self.elems,
+                                             self.mailboxes, self.part.rank, root, self.epoch,
+                                             stream)
+        if rc != 0:
+            raise RuntimeError(f"b2g_splitk_peer_reduce failed (status {rc})")
+
+    def close(self) -> None:
+        for r, ptr in enumerate(self.mailboxes):
+            if r != self.part.rank:
+                self.backend.peer_mailbox_close(ptr)
+        self.backend.peer_mailbox_destroy(self.own)
+        self.mailboxes = []
 
 
 def init_node(backend: str = "nccl", timeout_s: float = 60.0) -> Partitioner:

@@ -123,6 +123,13 @@ def _tri_useful(n):
     return 2.0 * n * (n + 1) * (n + 2) / 6.0
 
 
+def _tri_cost(n):
+    """Dense-equivalent flops, and the minimum bytes of a triangular product:
+    the two operand triangles read once and the whole n x n output written
+    (its masked triangle as zeros): 4 (n (n + 1) + n^2) bytes."""
+    return 2.0 * n * n * n, 4.0 * (n * (n + 1) + n * n)
+
+
 def _w(name, pid, shapes, seed, make, cost, bound, useful=0.0):
     flops, nbytes = cost
     return Workload(name, pid, shapes, seed, make, flops, nbytes, bound, useful)
@@ -137,6 +144,10 @@ def _add(w: Workload):
 
 # square
 _add(_w("square", 1, dict(m=2048, n=2048, k=2048), 0, _mk_nn, _gemm_cost(2048, 2048, 2048), "tensor"))
+# Reference PID 2 (no benchmark config): its kernel hard-codes M = 2048,
+# K = 8192, N = 4096 (kernels/2_Standard_matrix_multiplication_best_kernel.cu:16-18).
+_add(_w("standard", 2, dict(m=2048, n=4096, k=8192), 19, _mk_nn, _gemm_cost(2048, 4096, 8192),
+        "tensor"))
 # transposed operands, M=1024, K=4096, N=2048
 _add(_w("transposed_a", 16, dict(m=1024, n=2048, k=4096), 1, _mk_tn, _gemm_cost(1024, 2048, 4096), "tensor"))
 _add(_w("transposed_b", 17, dict(m=1024, n=2048, k=4096), 2, _mk_nt, _gemm_cost(1024, 2048, 4096), "tensor"))
@@ -154,9 +165,9 @@ _add(_w("irregular", 8, dict(m=8205, n=5921, k=2949), 9, _mk_nn, _gemm_cost(8205
 # structured operands at N=4096, and the 4-D product
 _add(Workload("diag", 12, dict(n=4096), 10, _mk_diag, 4096.0 * 4096,
               4.0 * (4096 + 2 * 4096 * 4096), "hbm"))
-_add(_w("upper_tri", 14, dict(n=4096), 11, _mk_upper, _gemm_cost(4096, 4096, 4096), "tensor",
+_add(_w("upper_tri", 14, dict(n=4096), 11, _mk_upper, _tri_cost(4096), "tensor",
         _tri_useful(4096)))
-_add(_w("lower_tri", 15, dict(n=4096), 12, _mk_lower, _gemm_cost(4096, 4096, 4096), "tensor",
+_add(_w("lower_tri", 15, dict(n=4096), 12, _mk_lower, _tri_cost(4096), "tensor",
         _tri_useful(4096)))
 _add(_w("symmetric", 13, dict(n=4096), 13, _mk_sym, _gemm_cost(4096, 4096, 4096), "tensor"))
 _add(_w("tensor4d", 11, dict(b=16, i=256, j=512, l=256, k=768), 14, _mk_4d,
@@ -199,7 +210,7 @@ def cost_for(name: str, **shapes) -> Tuple[float, float]:
     w = WORKLOADS[name]
     s = dict(w.shapes)
     s.update(shapes)
-    if name in ("square", "transposed_a", "transposed_b", "transposed_b", "transposed_both",
+    if name in ("square", "standard", "transposed_a", "transposed_b", "transposed_both",
                 "small_k", "large_k", "tall_skinny", "irregular"):
         return _gemm_cost(s["m"], s["n"], s["k"])
     if name == "batched":
@@ -220,6 +231,8 @@ def cost_for(name: str, **shapes) -> Tuple[float, float]:
     if name == "sdpa":
         return _sdpa_cost(s["batch"], s["heads"], s["seq"], s["dim"])
     n = s["n"]
+    if name in ("upper_tri", "lower_tri"):
+        return _tri_cost(n)
     return _gemm_cost(n, n, n)
 
 
@@ -236,7 +249,7 @@ def device_inputs(w: Workload, seed_offset: int = 0, device="cuda", **override):
     s.update(override)
     r = lambda *sh: torch.randn(*sh, generator=g, device=device, dtype=torch.float32)
     n = w.name
-    if n in ("square", "small_k", "large_k", "tall_skinny", "irregular"):
+    if n in ("square", "standard", "small_k", "large_k", "tall_skinny", "irregular"):
         return r(s["m"], s["k"]), r(s["k"], s["n"])
     if n == "transposed_a":
         return r(s["k"], s["m"]), r(s["k"], s["n"])

@@ -32,6 +32,7 @@
  *   kernels/5_Matrix_scalar_multiplication_best_kernel.cu:47    matrix_scalar_mult_cuda  -> b2g_scale
  *   kernels/87_conv_pointwise_2D_best_kernel.cu:451             pointwise_conv_cuda      -> b2g_pointwise_conv
  *   kernels/97_ScaledDotProductAttention_best_kernel.cu:256     fused_attention_cuda     -> b2g_sdpa
+ *   kernels/6_Matmul_with_large_K_dimension_best_kernel.cu:147-200 (streams + C.add_) -> b2g_splitk_peer_reduce
  *
  * Error behaviour: every entry point returns a b2g_status; 0 is success.
  * Nothing traps or asserts on the device.  Kernel-side waits are bounded;
@@ -227,6 +228,43 @@ B2G_API int b2g_pointwise_conv(const float* in, const float* weight, const float
  */
 B2G_API int b2g_sdpa(const void* q, const void* k, const void* v, void* out, int64_t batch,
                      int64_t heads, int64_t seq, int64_t dim, float scale, b2g_stream_t stream);
+
+/*
+ * Cross-GPU sum of a K split (one process per GPU on one node).
+ *
+ * Replaces the partial-sum step of the reference's large-K product, which
+ * splits K over 8 streams of one GPU and adds the partials with 7 C.add_
+ * calls (kernels/6_Matmul_with_large_K_dimension_best_kernel.cu:147-200).
+ * Here each rank multiplies its K slice with b2g_gemm and then calls
+ * b2g_splitk_peer_reduce on the same stream: a non-root rank copies its
+ * partial into a landing slot of the root's mailbox through the peer
+ * mapping (plain stores over NVLink) and stamps a per-chunk flag; the root
+ * waits (bounded) for every chunk from every rank and adds them, in rank
+ * order, into `out`, which already holds its own partial.  C = sum of the
+ * partials lands on the root only.
+ *
+ * Mailboxes: each rank creates one (b2g_peer_mailbox_create, device memory
+ * of b2g_peer_mailbox_bytes(elems, world)), shares its IPC handle with the
+ * others (any host channel), and opens theirs (b2g_peer_mailbox_open);
+ * `mailboxes[r]` is rank r's mailbox as mapped in the calling process (its
+ * own pointer for r == rank).  All ranks call with the same epoch, 1, 2, 3,
+ * ... per mailbox set; a rank may run at most one epoch ahead of the root
+ * (it waits, bounded, for the root to free the landing slot).  A wait that
+ * gives up records 0x201 (slot credit) or 0x202 (chunk not ready) in the
+ * device error word (b2g_read_device_error) and the call's output is
+ * incomplete.  partial / out: elems fp32, 16-byte aligned.
+ */
+#define B2G_PEER_MAX_RANKS 16
+typedef struct b2g_ipc_handle { unsigned char bytes[64]; } b2g_ipc_handle;
+B2G_API int64_t b2g_peer_mailbox_bytes(int64_t elems, int world);
+B2G_API int b2g_peer_mailbox_create(int64_t elems, int world, void** mailbox,
+                                    b2g_ipc_handle* handle);
+B2G_API int b2g_peer_mailbox_open(const b2g_ipc_handle* handle, void** mailbox);
+B2G_API int b2g_peer_mailbox_close(void* mailbox);     /* a mailbox opened from a handle */
+B2G_API int b2g_peer_mailbox_destroy(void* mailbox);   /* a mailbox this process created */
+B2G_API int b2g_splitk_peer_reduce(const float* partial, float* out, int64_t elems,
+                                   void* const* mailboxes, int world, int rank, int root,
+                                   int64_t epoch, b2g_stream_t stream);
 
 /* Read and clear the device-side error word of `device` (synchronises it). */
 B2G_API int b2g_read_device_error(int device, int32_t* code);

@@ -24,8 +24,19 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-REF_ROOT = Path(os.environ.get("B2G_REFERENCE_ROOT", "/root/reference"))
-KERNELS = REF_ROOT / "kernels"
+# Root of the reference checkout (the directory holding kernels/): the
+# B2G_REFERENCE_ROOT environment variable, or the first command-line
+# argument of this script.  Unset: nothing is built (reference_available()
+# is False), and load() still imports modules built earlier.
+REF_ROOT = Path(os.environ["B2G_REFERENCE_ROOT"]) if os.environ.get("B2G_REFERENCE_ROOT") else None
+KERNELS = REF_ROOT / "kernels" if REF_ROOT else None
+
+
+def set_reference_root(path) -> None:
+    """Point the builder at a reference checkout (the directory with kernels/)."""
+    global REF_ROOT, KERNELS
+    REF_ROOT = Path(path)
+    KERNELS = REF_ROOT / "kernels"
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
 # PID -> (file, Part-3 function name, file:line of that function)
@@ -56,7 +67,7 @@ EXT = sysconfig.get_config_var("EXT_SUFFIX")
 
 
 def reference_available() -> bool:
-    return KERNELS.is_dir()
+    return KERNELS is not None and KERNELS.is_dir()
 
 
 def module_path(pid: int) -> Path:
@@ -149,5 +160,8 @@ def load(pid: int):
 
 
 if __name__ == "__main__":
+    args = [a for a in sys.argv[1:] if not a.startswith("-")]
+    if args:
+        set_reference_root(args[0])
     for p in build_all(verbose="-v" in sys.argv, force="--force" in sys.argv):
         print(p)

@@ -20,7 +20,7 @@ The configs reach the code paths small shapes do not: the dynamic unit
 schedule with thousands of units (its unit ring wraps many times), batched
 units on the dynamic schedule, output offsets past 2^31 bytes, the
 triangular unit table with split K pieces, and split-K over 74 pieces.
-Reference sites: kernels/1_...:189, 3_...:113, 6_...:128, 7_...:80,
+Reference sites: kernels/1_...:189, 2_...:16-18,117, 3_...:113, 6_...:128, 7_...:80,
 8_...:155, 9_...:145, 10_...:180, 11_...:132,165, 13_...:134, 14_...:135,
 15_...:155, 16_...:124, 17_...:267, 18_...:152.
 """
@@ -35,7 +35,7 @@ pytestmark = pytest.mark.gpu
 
 TOL = O.TOL
 MODES = ["tf32", "3xtf32"]
-CONFIGS = ["square", "transposed_a", "transposed_b", "transposed_both", "batched", "tensor3d",
+CONFIGS = ["square", "standard", "transposed_a", "transposed_b", "transposed_both", "batched", "tensor3d",
            "small_k", "large_k", "tall_skinny", "irregular", "upper_tri", "lower_tri",
            "symmetric", "tensor4d"]
 
@@ -68,7 +68,8 @@ def full_check(name, A, B, C):
     """Relative Frobenius norm of all of C against a float64 GPU product."""
     f = Fro()
     d = torch.float64
-    if name in ("square", "small_k", "large_k", "tall_skinny", "irregular", "symmetric"):
+    if name in ("square", "standard", "small_k", "large_k", "tall_skinny", "irregular",
+                "symmetric"):
         Bd = B.to(d)
         for r0, r1 in _chunks(A.shape[0], 2048):
             f.add(C[r0:r1], A[r0:r1].to(d) @ Bd)
@@ -108,8 +109,8 @@ def full_check(name, A, B, C):
 def sample_check(name, A, B, C):
     """Relative Frobenius norm of a sampled subset of C against the CPU oracle."""
     errs = []
-    if name in ("square", "small_k", "large_k", "tall_skinny", "irregular", "symmetric",
-                "transposed_b"):
+    if name in ("square", "standard", "small_k", "large_k", "tall_skinny", "irregular",
+                "symmetric", "transposed_b"):
         m = A.shape[0]
         rows = _sample_rows(m, 512)
         ref = O.BY_PID[_pid(name)](_np(A[rows]), _np(B))

@@ -12,7 +12,7 @@ def _h():
     return import_pkg("harness")
 
 
-@pytest.mark.parametrize("pid", [1, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 87, 97])
+@pytest.mark.parametrize("pid", [1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 87, 97])
 def test_model_ref_matches_oracle(pid):
     h = _h()
     assert pid in h.pids()
@@ -26,7 +26,7 @@ def test_model_ref_matches_oracle(pid):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("pid", [1, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 87, 97])
+@pytest.mark.parametrize("pid", [1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16, 17, 18, 87, 97])
 def test_model_new_matches_model_ref(pid):
     h = _h()
     ok, err = h.check(pid, *h.inputs(pid, small=True))

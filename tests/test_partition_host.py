@@ -74,6 +74,16 @@ def _worker(rank, world, port, scenario, q):
             r0, r1 = p.batch_range(M)
             full = p.gather_rows(A[r0:r1] * 2, M)
             q.put(("gather", rank, float((full - 2 * A).abs().max())))
+        elif scenario == "peer_orchestration":
+            fake = FakePeerBackend(rank)
+            red = p.peer_reducer(M * N, backend=fake)
+            assert p.peer_reducer(M * N, backend=fake) is red      # one mailbox set per size
+            part_t = torch.zeros(M, N)
+            for _ in range(2):
+                red.reduce(None, part_t, root=0) if rank == 0 else \
+                    red.reduce(part_t, None, root=0)
+            red.close()
+            q.put(("peer", rank, red.epoch, fake.calls, fake.closed, fake.destroyed))
         elif scenario == "dead_peer":
             if rank == 1:
                 os._exit(3)          # leaves between steps, nothing in flight
@@ -87,6 +97,33 @@ def _worker(rank, world, port, scenario, q):
     finally:
         if scenario != "dead_peer":
             dist.destroy_process_group()
+
+
+class FakePeerBackend:
+    """Stand-in for the C-ABI mailbox calls: pointers 1000 + rank for a rank's
+    own mailbox, 2000 + rank for a peer's opened from its handle."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.calls = []
+        self.closed = []
+        self.destroyed = []
+
+    def peer_mailbox_create(self, elems, world):
+        return 1000 + self.rank, f"mailbox-of-{self.rank}".encode().ljust(64, b"\0")
+
+    def peer_mailbox_open(self, handle):
+        return 2000 + int(handle.rstrip(b"\0").decode().split("-")[-1])
+
+    def peer_mailbox_close(self, ptr):
+        self.closed.append(ptr)
+
+    def peer_mailbox_destroy(self, ptr):
+        self.destroyed.append(ptr)
+
+    def splitk_peer_reduce(self, partial, out, elems, mailboxes, rank, root, epoch, stream):
+        self.calls.append((bool(partial), bool(out), elems, list(mailboxes), rank, root, epoch))
+        return 0
 
 
 def _run(scenario, world=2, timeout=60):
@@ -128,3 +165,25 @@ def test_dead_peer_surfaces_as_error_not_hang():
     res = [o for o in out if o[0] in ("error", "no_error")]
     assert res and res[0][0] == "error", res
     assert res[0][1] < 60
+
+
+def test_peer_reducer_exchanges_handles_and_counts_epochs():
+    """The peer-memory reduction's host side on gloo ranks: IPC handles go
+    round with all_gather_object, each rank's table lists every mailbox in
+    rank order (its own pointer, the others opened from their handles), all
+    ranks call with the same epochs, the root passes `out` and the others
+    `partial`, and close() unmaps the peers' mailboxes and frees its own."""
+    out, codes = _run("peer_orchestration")
+    assert codes == [0, 0]
+    res = {o[1]: o for o in out if o[0] == "peer"}
+    assert set(res) == {0, 1}
+    M, N = 24, 17
+    for rank, (_, _, epoch, calls, closed, destroyed) in res.items():
+        assert epoch == 2
+        table = [1000, 2001] if rank == 0 else [2000, 1001]
+        assert [c[6] for c in calls] == [1, 2]
+        for partial, outp, elems, mbs, r, root, _ in calls:
+            assert elems == M * N and mbs == table and r == rank and root == 0
+            assert (partial, outp) == ((False, True) if rank == 0 else (True, False))
+        assert closed == [t for i, t in enumerate(table) if i != rank]
+        assert destroyed == [1000 + rank]
