@@ -76,9 +76,9 @@ __device__ __forceinline__ bool wait_at_least(const uint64_t* flag, uint64_t wan
                                               long long limit_ns) {
   if (ld_acquire_sys(flag) >= want) return true;
   const uint64_t t0 = b2g::ptx::globaltimer_ns();
-  while (ld_acquire_sys(flag) < want) {
+  for (unsigned spin = 0; ld_acquire_sys(flag) < want; ++spin) {
     if (b2g::ptx::globaltimer_ns() - t0 > static_cast<uint64_t>(limit_ns)) return false;
-    __nanosleep(64);
+    if (spin > 64) __nanosleep(32);   // poll tight first: the flag usually lands within ~1 us
   }
   return true;
 }
@@ -93,21 +93,28 @@ __global__ void __launch_bounds__(kThreads) peer_push_kernel(const float* __rest
                                                              Layout lay, int world, int rank,
                                                              int root, long long epoch,
                                                              long long limit_ns, int* err) {
-  // The partial was written by the preceding GEMM (programmatic launch).
-  b2g::ptx::griddep_wait();
+  // Let the stream's next kernel (the next GEMM) launch and do its set-up
+  // now; it waits for this grid to finish before it touches memory.
+  b2g::ptx::griddep_launch_dependents();
   __shared__ int abort_flag;
   const int64_t c = blockIdx.x;
   unsigned char* mine = args.mbox[rank];
   unsigned char* rootb = args.mbox[root];
   if (threadIdx.x == 0) {
     // The slot this epoch writes was last read by the root two epochs ago.
+    // (Waited for before the GEMM has finished: launched programmatically,
+    // this CTA polls while the GEMM's last units run.)
     const uint64_t* consumed = reinterpret_cast<const uint64_t*>(mine + lay.consumed_off) + c;
     const long long need = epoch - 2;
     abort_flag = (need > 0 && !wait_at_least(consumed, static_cast<uint64_t>(need), limit_ns));
-    if (abort_flag && err) atomicCAS(err, 0, kErrPeerCredit);
   }
+  // The partial was written by the preceding GEMM.
+  b2g::ptx::griddep_wait();
   __syncthreads();
-  if (abort_flag) return;
+  if (abort_flag) {
+    if (threadIdx.x == 0 && err) atomicCAS(err, 0, kErrPeerCredit);
+    return;
+  }
   float* dst = reinterpret_cast<float*>(rootb + lay.landing_off +
                                         ((epoch & 1) * world + rank) * lay.slot_stride);
   const int64_t i = c * kChunk + static_cast<int64_t>(threadIdx.x) * 4;
@@ -117,8 +124,9 @@ __global__ void __launch_bounds__(kThreads) peer_push_kernel(const float* __rest
   } else {
     for (int64_t j = i; j < elems; ++j) dst[j] = __ldcg(partial + j);
   }
-  // Every thread's peer stores are ordered before the flag.
-  __threadfence_system();
+  // The CTA barrier orders every thread's peer stores before thread 0's
+  // release store (cumulative at system scope): one fence per chunk, not
+  // one per thread.
   __syncthreads();
   if (threadIdx.x == 0) {
     uint64_t* ready = reinterpret_cast<uint64_t*>(rootb + lay.ready_off) + c * world + rank;
@@ -133,14 +141,14 @@ __global__ void __launch_bounds__(kThreads) peer_reduce_kernel(float* __restrict
                                                                Layout lay, int world, int root,
                                                                long long epoch, long long limit_ns,
                                                                int* err) {
-  // out holds this rank's own partial, written by the preceding GEMM.
-  b2g::ptx::griddep_wait();
+  b2g::ptx::griddep_launch_dependents();   // as in peer_push_kernel
   __shared__ int abort_flag;
   const int64_t c = blockIdx.x;
   unsigned char* mine = args.mbox[root];
   if (threadIdx.x == 0) abort_flag = 0;
   __syncthreads();
   const int t = threadIdx.x;
+  // The other ranks' chunks (polled while this rank's GEMM may still run).
   if (t < world && t != root) {
     const uint64_t* ready = reinterpret_cast<const uint64_t*>(mine + lay.ready_off) + c * world + t;
     if (!wait_at_least(ready, static_cast<uint64_t>(epoch), limit_ns)) {
@@ -148,6 +156,8 @@ __global__ void __launch_bounds__(kThreads) peer_reduce_kernel(float* __restrict
       if (err) atomicCAS(err, 0, kErrPeerReady);
     }
   }
+  // out holds this rank's own partial, written by the preceding GEMM.
+  b2g::ptx::griddep_wait();
   __syncthreads();
   if (abort_flag) return;
   const float* slot = reinterpret_cast<const float*>(mine + lay.landing_off +

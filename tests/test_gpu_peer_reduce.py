@@ -1,12 +1,13 @@
 """The cross-GPU K-split sum (b2g_splitk_peer_reduce) on the GPU.
 
 * One GPU, protocol only: two mailboxes on one device stand for rank 0
-  (root) and rank 1.  Every call runs on one stream in order (rank 1's push,
-  then the root's reduce), so no kernel ever waits for another kernel
-  running beside it; the flags a kernel waits on were set by a kernel that
-  finished before it.  Several epochs run back to back (the landing slots
-  alternate, the credits advance), and the sum is checked bit for bit
-  (out = P0 + P1 in fp32) and against the fp64 oracle.
+  (root) and rank 1.  The device is synchronised after each emulated
+  rank's call (rank 1's push, then the root's reduce), so no kernel ever
+  waits for another kernel running beside it: the flags a kernel waits on
+  were set by a kernel that had finished before it was launched.  Several
+  epochs run one after another (the landing slots alternate, the credits
+  advance), and the sum is checked bit for bit (out = P0 + P1 in fp32) and
+  against the fp64 oracle.
 * One GPU, bounded wait: the root reduces an epoch nobody pushed (a flag
   that nothing sets); with B2G_WAIT_LIMIT_MS=50 the wait gives up, the
   kernel records 0x202 in the device error word and returns, and the next
@@ -45,6 +46,7 @@ def test_peer_reduce_protocol_on_one_gpu(capi, ops):
             P1 = ops.p2.forward(A[:, h:].contiguous(), B[h:].contiguous())
             rc = capi.splitk_peer_reduce(P1.data_ptr(), 0, elems, mb, 1, 0, epoch, stream)
             assert rc == capi.B2G_OK, capi.status_string(rc)
+            torch.cuda.synchronize()          # rank 1's push has finished
             out = ops.p2.forward(A[:, :h].contiguous(), B[:h].contiguous())
             P0 = out.clone()
             rc = capi.splitk_peer_reduce(0, out.data_ptr(), elems, mb, 0, 0, epoch, stream)
