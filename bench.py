@@ -427,6 +427,8 @@ def main():
     ap.add_argument("--profile-case", default="",
                     help="run only this workload (name) for --steps calls, untimed: the "
                          "command an ncu capture of one config wraps")
+    ap.add_argument("--profile-impl", choices=["ours", "cublas"], default="ours",
+                    help="--profile-case: our operator or the same math through cuBLAS")
     ap.add_argument("--set", action="append", default=[],
                     help="dim=value override of the --profile-case workload's shape")
     ap.add_argument("--no-e2e", action="store_true")
@@ -544,11 +546,15 @@ def profile_case(W, args):
     w = W[args.profile_case]
     over = {k: int(v) for k, v in (x.split("=") for x in args.set)}
     ins = device_inputs(w, **over)
-    op = ops.OPERATORS[w.pid].forward
+    if args.profile_impl == "cublas":
+        op = lambda *a: cublas_fn(w.name, *a)()
+    else:
+        op = ops.OPERATORS[w.pid].forward
     for _ in range(args.warmup + args.steps):
         op(*ins)
         torch.cuda.synchronize()
-    print(json.dumps({"profile_case": w.name, "shapes": dict(w.shapes, **over),
+    print(json.dumps({"profile_case": w.name, "impl": args.profile_impl,
+                      "shapes": dict(w.shapes, **over),
                       "calls": args.warmup + args.steps,
                       "device_error": ops.read_device_error(torch.cuda.current_device())}))
 

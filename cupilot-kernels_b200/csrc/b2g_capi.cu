@@ -110,6 +110,61 @@ long long wait_limit_ns() {
   return ns;
 }
 
+// Tuning overrides of the dispatcher: B2G_TILE=pair512|pair256|pair128|
+// single256|single128 pins the tile shape, B2G_SPLITS=n the split-K factor
+// of plain GEMMs.  Read once per process, or at every call when the process
+// started with B2G_TUNING=1 (sweeps that change them between calls).
+bool tuning_mode() {
+  static const bool on = [] {
+    const char* e = std::getenv("B2G_TUNING");
+    return e && *e == '1';
+  }();
+  return on;
+}
+const char* tile_override() {
+  static const char* once = std::getenv("B2G_TILE");
+  return tuning_mode() ? std::getenv("B2G_TILE") : once;
+}
+int splits_override() {
+  auto read = [] {
+    const char* e = std::getenv("B2G_SPLITS");
+    return (e && *e) ? std::atoi(e) : 0;
+  };
+  static const int once = read();
+  return tuning_mode() ? read() : once;
+}
+
+// Longest K piece of a triangular unit table, in percent of the mean load
+// per cluster (B2G_TRI_SPLIT; a tuning knob, read like the overrides above).
+int64_t tri_split_pct() {
+  auto read = [] {
+    const char* e = std::getenv("B2G_TRI_SPLIT");
+    const int v = (e && *e) ? std::atoi(e) : 0;
+    return v > 0 ? v : 100;
+  };
+  static const int once = read();
+  return tuning_mode() ? read() : once;
+}
+
+// Triangular units run 8 epilogue warps (B2G_TRI_EPIW=4 selects 4; a
+// tuning knob, read like the overrides above).
+bool tri_epiw8() {
+  auto read = [] {
+    const char* e = std::getenv("B2G_TRI_EPIW");
+    return !(e && std::atoi(e) == 4);
+  };
+  static const bool once = read();
+  return tuning_mode() ? read() : once;
+}
+
+// B2G_TRACE_PTR=<device address of 16 u64 per CTA> (tuning mode only): the
+// engine writes its per-CTA phase stamps there (EngineParams::trace).
+unsigned long long* trace_pointer() {
+  if (!tuning_mode()) return nullptr;
+  const char* e = std::getenv("B2G_TRACE_PTR");
+  return (e && *e) ? reinterpret_cast<unsigned long long*>(std::strtoull(e, nullptr, 0)) : nullptr;
+}
+
 int take_injected_stall() {
   static std::atomic<int> armed{-1};
   int v = armed.load();
@@ -531,7 +586,9 @@ TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int t
     tiles[t] = decode_unit(q, t);
     total += tiles[t].kb_hi - tiles[t].kb_lo;
   }
-  const int64_t lmax = allow_split ? std::max<int64_t>(8, cdiv(total, clusters)) : (1ll << 40);
+  const int64_t lmax = allow_split
+                           ? std::max<int64_t>(8, cdiv(total * tri_split_pct(), clusters * 100ll))
+                           : (1ll << 40);
   TriTable out;
   for (const WorkUnit& u : tiles) {
     const int len = u.kb_hi - u.kb_lo;
@@ -585,10 +642,11 @@ TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int t
 std::shared_ptr<const TriTable> cached_tri_table(const b2g_gemm_desc* d, int block_m,
                                                  int block_n, int tiles_m, int tiles_n,
                                                  int clusters, bool allow_split) {
-  using Key = std::tuple<int64_t, int64_t, int, int, int, int, int, int, int>;
+  using Key = std::tuple<int64_t, int64_t, int, int, int, int, int, int, int, int>;
   static std::mutex mu;
   static std::map<Key, std::shared_ptr<const TriTable>> cache;
-  const Key key{d->m, d->k, d->op, block_m, block_n, tiles_m, tiles_n, clusters, allow_split};
+  const Key key{d->m,    d->k,    d->op,    block_m,     block_n,
+                tiles_m, tiles_n, clusters, allow_split, tri_split_pct()};
   {
     std::lock_guard<std::mutex> lk(mu);
     auto it = cache.find(key);
@@ -687,6 +745,8 @@ void choose_splits(const b2g_gemm_desc* d, int64_t slots, int64_t kb_total, int 
   int64_t s = 1;
   if (d->op == B2G_OP_GEMM && slots > 0 && slots * 4 < num_sms * 3 && kb_total >= 16)
     s = std::max<int64_t>(1, std::min<int64_t>(num_sms / slots, kb_total / 8));
+  const int forced = splits_override();
+  if (d->op == B2G_OP_GEMM && forced > 0) s = std::min<int64_t>(forced, std::max<int64_t>(kb_total, 1));
   *kbps = std::max<int64_t>(1, cdiv(kb_total, s));
   *splits = std::max<int64_t>(1, cdiv(kb_total, *kbps));
 }
@@ -700,7 +760,7 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   const int64_t kb_total = cdiv(d->k, kBlockK);
   const int64_t batch = d->batch;
   int bn = 256, ctas = 1;
-  static const char* forced = std::getenv("B2G_TILE");
+  const char* forced = tile_override();
   // Triangular NN operands take the plain engine with diagonal-block copies
   // (no transform warps); other triangular layouts mask in the transform warps.
   const bool tri_diag = d->op != B2G_OP_GEMM && !x3 && !d->trans_a && !d->trans_b;
@@ -993,6 +1053,7 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.diag_oob_row = static_cast<int>(d->m);
   p.row_bias = row_bias;
   p.err = err_word;
+  p.trace = trace_pointer();
   // Dynamic schedule: plain GEMMs with more units than CTAs (pairs), every
   // unit holding at least one K block (no structurally empty units).
   const int64_t slots = pl.grid / pl.cluster_ctas;
@@ -1088,7 +1149,7 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   if (pl.cluster_ctas == 2) {
     if (pl.block_n == 512)
       return launch_majors<512, 4, false, false, true>(a_mn, b_mn, maps, p, grid, stream);
-    if (pl.block_n == 256 && p.kb_per_split >= 16)
+    if (pl.block_n == 256 && p.kb_per_split >= 16 && !(p.tri != kTriNone && tri_epiw8()))
       // Long K loops: 4 epilogue warps drain a unit well inside the next
       // unit's mainloop and compete less with it (bmm 128 x 512x2048x1024:
       // +7 % in bursts, +2 % sustained under the power cap).

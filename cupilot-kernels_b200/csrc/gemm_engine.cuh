@@ -82,6 +82,13 @@ struct EngineParams {
   unsigned* tile_flags;
   unsigned epoch;
   int* err;
+  // Tuning aid (null in normal use): per CTA, 16 globaltimer stamps at
+  // trace[cta * 16 + i]: 0 entry, 1 after the grid-dependency wait, 2 first
+  // operand stage landed (MMA warp), 3 last MMA issued, 4 first accumulator
+  // ready (epilogue warp 0), 5 last store issued (epilogue warp 0), 6 exit,
+  // 7 tile flag seen (split-K), 8.. epilogue warp 0's chunk groups of its
+  // last unit: TMEM data in registers, store issued (pairs of stamps).
+  unsigned long long* trace;
 };
 
 constexpr int kFlagSlots = 16;     // epilogue warps per tile (8 per CTA, a pair)
@@ -548,6 +555,8 @@ __global__ void __launch_bounds__(
   units.step = unit_step;
   units.dyn = p.sched != nullptr;
 
+  unsigned long long* trace = p.trace ? p.trace + static_cast<size_t>(blockIdx.x) * 16 : nullptr;
+  if (trace && threadIdx.x == 0) trace[0] = ptx::globaltimer_ns();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(&full[s], 1);
@@ -591,6 +600,7 @@ __global__ void __launch_bounds__(
   // loads, unit tables, counters, output) comes after this wait.
   ptx::griddep_launch_dependents();
   ptx::griddep_wait();
+  if (trace && threadIdx.x == 0) trace[1] = ptx::globaltimer_ns();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -804,6 +814,7 @@ __global__ void __launch_bounds__(
             ok = false;
             break;
           }
+          if (trace && it == 0) trace[2] = ptx::globaltimer_ns();
           ptx::tc_fence_after();
           const uint32_t sa = ptx::smem_addr(smem + Cfg::kOffA + s * Cfg::kABytes);
           const uint32_t sb = ptx::smem_addr(smem + Cfg::kOffB + s * Cfg::kBBytes);
@@ -845,6 +856,7 @@ __global__ void __launch_bounds__(
             ptx::mma_commit(&empty[s]);
         }
         if (!ok) break;
+        if (trace) trace[3] = ptx::globaltimer_ns();
         if (!p.inject_stall) {
           if (PAIR)
             ptx::mma_commit_pair(&tmem_full[buf], 0x3);
@@ -959,6 +971,7 @@ __global__ void __launch_bounds__(
         if (lane == 0) record_error(p.err, abort_flag, kErrWaitTmemFull);
         break;
       }
+      if (trace && ew == 0 && lane == 0 && tl == 0) trace[4] = ptx::globaltimer_ns();
       ptx::tc_fence_after();
       if (tile_flag != nullptr && u.kb_lo != 0 && row0 < p.M) {
         // Later K piece: its reduce-adds land on chunks the first piece zeroes.
@@ -978,6 +991,7 @@ __global__ void __launch_bounds__(
           if (lane == 0) record_error(p.err, abort_flag, kErrWaitZero);
           break;
         }
+        if (trace && ew == 0 && lane == 0) trace[7] = ptx::globaltimer_ns();
       }
       auto release = [&]() {
         ptx::tc_fence_before();
@@ -1028,6 +1042,7 @@ __global__ void __launch_bounds__(
           for (int g = 0; g < G; ++g)
 #pragma unroll
             for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[g][i]));
+          if (trace && ew == 0 && lane == 0 && g0 < 4) trace[8 + 2 * g0] = ptx::globaltimer_ns();
           if (with_bias) {
 #pragma unroll
             for (int g = 0; g < G; ++g)
@@ -1040,6 +1055,7 @@ __global__ void __launch_bounds__(
                                           r, ng, u.b, row0, col0, lane, u.accumulate);
           else
             store_group_tma<G>(p, &map_c, stg, r, ng, u.b, row0, col0, lane, u.accumulate);
+          if (trace && ew == 0 && lane == 0 && g0 < 4) trace[9 + 2 * g0] = ptx::globaltimer_ns();
         }
       } else if (row0 < p.M && half < nch) {
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + buf * BN;
@@ -1068,6 +1084,7 @@ __global__ void __launch_bounds__(
       } else {
         release();
       }
+      if (trace && ew == 0 && lane == 0) trace[5] = ptx::globaltimer_ns();
       ++tl;
     }
     if (lane == 0) ptx::bulk_wait_read<0>();   // staging boxes read before the CTA exits
@@ -1130,6 +1147,7 @@ __global__ void __launch_bounds__(
   ptx::tc_fence_before();
   __syncthreads();
   if (PAIR) ptx::cluster_sync();   // no CTA leaves while its peer may still signal it
+  if (trace && threadIdx.x == 0) trace[6] = ptx::globaltimer_ns();
   if (warp == 1) {
     ptx::tc_fence_after();
     if (PAIR)
