@@ -7,14 +7,21 @@ can regenerate them bit-for-bit), runs the reference's Part-3 function and
 stores its output (row subsets for the larger ones).  Shapes stay inside
 each reference kernel's own contract (tile multiples, K7's K = 64, K9's
 inner dimension <= 32, K87's channel and tile multiples, K16's block swizzle needing M and N multiples of 512,
-kernels/16_Matmul_with_transposed_A_best_kernel.cu:18-40).  K2 is skipped: its shape is hard-coded
-(kernels/2_Standard_matrix_multiplication_best_kernel.cu:16-18).  K4 is
-not run: its first call here (M = 96, K = 1024) raised an illegal memory
-access on a B200 although reading its kernel shows no out-of-range index at
-that shape, so it stays off the GPU; PID 4 is pinned by its closed-form
-known answer.
+kernels/16_Matmul_with_transposed_A_best_kernel.cu:18-40).  K2 runs at its
+own hard-coded 2048 x 8192 x 4096 (kernels/2_Standard_matrix_multiplication_best_kernel.cu:16-18)
+and keeps a 16 x 512 corner of its output.  K4 runs only where its loop
+bound cannot wrap: `num_vectors - blockDim.x*3` (kernels/4_Matrix_vector_multiplication_best_kernel.cu:22)
+mixes int with unsigned, so below 3072 float4s per row (K < 12288 at its
+1024 threads) the bound becomes a huge unsigned value and the loop reads
+past the row (its first call here, at K = 1024, raised an illegal memory
+access); K = 16384 is inside its contract.  Case 114 is K14 on UNMASKED
+inputs: K14 masks its own operands (kernels/14_...:74-75,84-85), which
+the oracle's triu(triu(A) triu(B)) must reproduce.
 
-    python tests/golden/make_reference_vectors.py
+    python tests/golden/make_reference_vectors.py [pid,pid,...]
+
+With a list of problem IDs only those cases are (re)generated and merged
+into the existing fixture.
 """
 import sys
 from pathlib import Path
@@ -25,10 +32,13 @@ import torch
 REPO = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(REPO))
 
-# pid -> (list of input shapes, rows of the output to keep); at most 64 rows
-# are stored to keep the fixture small.
+# case -> (list of input shapes, part of the output to keep: leading rows, or
+# a (rows, cols) corner); at most 64 rows are stored to keep the fixture small.
 SCALE = 2.5   # the scalar operand of K5
 CASES = {
+    2: ([(2048, 8192), (8192, 4096)], (16, 512)),   # K2's hard-coded shape; corner kept
+    4: ([(64, 16384), (16384, 1)], 64),
+    114: ([(256, 256), (256, 256)], 64),            # K14 on unmasked inputs
     5: ([(64, 256)], 64),
     1: ([(256, 256), (256, 256)], 64),
     3: ([(2, 256, 64), (2, 64, 256)], 64),
@@ -56,6 +66,8 @@ CASES = {
     97: ([(1, 1, 512, 1024)] * 3, 16),
 }
 SEED0 = 1234
+# Case -> the reference kernel (problem ID) it runs.
+KERNEL = {114: 14}
 
 
 def inputs(pid):
@@ -75,21 +87,33 @@ def inputs(pid):
     return ts
 
 
+def keep_part(C, keep):
+    """The stored part of an output: leading rows (int) or a leading
+    (rows, cols) corner of every output matrix."""
+    if keep is None:
+        return C
+    if isinstance(keep, tuple):
+        return C[..., : keep[0], : keep[1]]
+    return C[..., :keep, :]
+
+
 def main():
     from oracle import build_ref
 
-    out = {}
+    path = Path(__file__).with_name("reference_outputs.npz")
+    only = {int(x) for x in sys.argv[1].split(",")} if len(sys.argv) > 1 else None
+    out = dict(np.load(path)) if (only and path.exists()) else {}
     for pid, (_, keep) in CASES.items():
-        f = build_ref.load(pid)
+        if only and pid not in only:
+            continue
+        f = build_ref.load(KERNEL.get(pid, pid))
         A, B, *rest = inputs(pid)
         C = f(A.cuda(), B if pid == 5 else B.cuda(), *[t.cuda() for t in rest])
         torch.cuda.synchronize()
-        C = C.cpu().numpy()
-        if keep is not None:
-            C = C[..., :keep, :]                 # leading rows of every output matrix
+        C = keep_part(C.cpu().numpy(), keep)
         out[f"p{pid}"] = C.astype(np.float32)   # (fp16 outputs are exact in fp32)
         print(pid, C.shape, flush=True)
-    np.savez_compressed(Path(__file__).with_name("reference_outputs.npz"), **out)
+    np.savez_compressed(path, **out)
 
 
 if __name__ == "__main__":
