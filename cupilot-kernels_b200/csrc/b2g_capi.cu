@@ -146,6 +146,18 @@ int64_t tri_split_pct() {
   return tuning_mode() ? read() : once;
 }
 
+// B2G_TRI_PATH=gate: untransposed triangular products through the gated
+// transform warps instead of diagonal-block copies (tuning and comparison;
+// read like the overrides above).
+bool tri_path_gate() {
+  auto read = [] {
+    const char* e = std::getenv("B2G_TRI_PATH");
+    return e && std::strcmp(e, "gate") == 0;
+  };
+  static const bool once = read();
+  return tuning_mode() ? read() : once;
+}
+
 // Triangular units run 8 epilogue warps (B2G_TRI_EPIW=4 selects 4; a
 // tuning knob, read like the overrides above).
 bool tri_epiw8() {
@@ -561,6 +573,13 @@ int launch_majors(bool a_mn, bool b_mn, const CUtensorMap (&m)[5], const EngineP
 struct TriTable {
   std::vector<int4> units;
   std::vector<int2> split_tiles;
+  // What the engine reads (unit-table path without a pre-pass): the units,
+  // then one {tm, tn, 0, 0} entry per split tile.
+  std::vector<int4> device_image() const {
+    std::vector<int4> v(units);
+    for (const int2& t : split_tiles) v.push_back(make_int4(t.x, t.y, 0, 0));
+    return v;
+  }
 };
 
 TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int tiles_m,
@@ -577,7 +596,7 @@ TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int t
   q.kb_per_split = std::max(q.kb_total, 1);
   q.group_m = 8;
   q.tri = d->op == B2G_OP_TRI_UPPER ? kTriUpper : kTriLower;
-  struct Item { int tm, tn, lo, hi, flags, weight; };
+  struct Item { int tm, tn, lo, hi, flags, weight, slot; };
   std::vector<Item> items;
   const int64_t ntiles = static_cast<int64_t>(tiles_m) * tiles_n;
   int64_t total = 0;
@@ -593,15 +612,20 @@ TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int t
   for (const WorkUnit& u : tiles) {
     const int len = u.kb_hi - u.kb_lo;
     if (len == 0) {
-      items.push_back({u.tm, u.tn, 0, 0, 0, 3});   // zero tile: epilogue stores only
+      items.push_back({u.tm, u.tn, 0, 0, 0, 3, 0});   // zero tile: epilogue stores only
       continue;
     }
-    const int np = static_cast<int>(cdiv(len, lmax));
+    // Split tiles get a flag slot (the engine's in-kernel clear of split
+    // tiles has kFlagTiles of them); beyond that, tiles stay whole.
+    int np = static_cast<int>(cdiv(len, lmax));
+    if (np > 1 && static_cast<int>(out.split_tiles.size()) >= kFlagTiles) np = 1;
+    const int slot = np > 1 ? static_cast<int>(out.split_tiles.size()) + 1 : 0;
     if (np > 1) out.split_tiles.push_back(make_int2(u.tm, u.tn));
     for (int j = 0; j < np; ++j) {
       const int lo = u.kb_lo + static_cast<int>(static_cast<int64_t>(len) * j / np);
       const int hi = u.kb_lo + static_cast<int>(static_cast<int64_t>(len) * (j + 1) / np);
-      items.push_back({u.tm, u.tn, lo, hi, np > 1 ? kUnitAccumulate : 0, hi - lo + 2});
+      const int fl = np > 1 ? (kUnitAccumulate | (j == 0 ? kUnitFirst : 0)) : 0;
+      items.push_back({u.tm, u.tn, lo, hi, fl, hi - lo + 2, slot});
     }
   }
   std::stable_sort(items.begin(), items.end(),
@@ -629,7 +653,8 @@ TriTable build_tri_table(const b2g_gemm_desc* d, int block_m, int block_n, int t
   for (int c = 0; c < clusters; ++c)
     for (size_t r = 0; r < per[c].size(); ++r) {
       const Item& it = items[per[c][r]];
-      out.units[r * clusters + c] = make_int4(it.tm, it.tn, it.lo, it.hi | (it.flags << 24));
+      out.units[r * clusters + c] =
+          make_int4(it.tm | (it.slot << 16), it.tn, it.lo, it.hi | (it.flags << 24));
     }
   return out;
 }
@@ -761,9 +786,16 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
   const int64_t batch = d->batch;
   int bn = 256, ctas = 1;
   const char* forced = tile_override();
-  // Triangular NN operands take the plain engine with diagonal-block copies
-  // (no transform warps); other triangular layouts mask in the transform warps.
-  const bool tri_diag = d->op != B2G_OP_GEMM && !x3 && !d->trans_a && !d->trans_b;
+  // Triangular TF32 products on untransposed operands: a pre-pass writes
+  // masked copies of the diagonal blocks that the engine's producer loads.
+  // Other layouts (and B2G_TRI_PATH=gate, a tuning knob) mask inside the
+  // engine: the K blocks that the diagonal crosses go through the transform
+  // warps, wholly masked boxes are TMA zero fill.  At N = 4096 the copies
+  // cost one 2-4 us pre-pass; gating costs a transform handshake on the
+  // MMA's path at every crossing block (58 vs 103 us measured).
+  const bool tri_diag = d->op != B2G_OP_GEMM && !x3 && !d->trans_a && !d->trans_b &&
+                        !tri_path_gate();
+  const bool tri_gate = d->op != B2G_OP_GEMM && !x3 && !tri_diag;
   // 3xTF32 on plain GEMMs: lo parts pre-split into workspace, loaded by TMA;
   // triangular 3xTF32 masks and splits in the (single-CTA) transform warps.
   const bool x3_split = x3 && d->op == B2G_OP_GEMM;
@@ -774,7 +806,7 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
     // vs 190 us for pairs, whose transform warps mask twice the tile).
     const bool force_single = forced && std::strncmp(forced, "single", 6) == 0;
     const bool force_pair = forced && std::strncmp(forced, "pair", 4) == 0;
-    if (d->m > kBlockM && !force_single && (x3_split || tri_diag || force_pair)) {
+    if (d->m > kBlockM && !force_single && (x3_split || tri_diag || tri_gate || force_pair)) {
       ctas = 2;
       bn = 256;
     } else {
@@ -870,6 +902,11 @@ extern "C" int b2g_gemm_plan_for(const b2g_gemm_desc* d, int num_sms, b2g_gemm_p
     ws += round_up(static_cast<int64_t>(tt->units.size()) * sizeof(int4), 256);
     ws += round_up(static_cast<int64_t>(tt->split_tiles.size()) * sizeof(int2), 256);
     pl->work_units = static_cast<int64_t>(tt->units.size());
+  } else if (tri_gate) {
+    // The unit table lives in a per-device cache (uploaded once per shape).
+    const auto tt = cached_tri_table(d, pl->block_m, pl->block_n, pl->tiles_m, pl->tiles_n,
+                                     pl->grid / ctas, pl->tma_store);
+    pl->work_units = static_cast<int64_t>(tt->units.size());
   }
   pl->workspace_bytes = ws;
   return B2G_OK;
@@ -898,8 +935,46 @@ extern "C" int64_t b2g_gemm_workspace_bytes(const b2g_gemm_desc* d) {
 // Everything a GEMM call does once its plan is known and its workspace
 // checked: staged copies of unaligned operands, tensor maps, split-K clear
 // of C, and the engine launch.
+// Device copies of triangular unit tables, per device, uploaded once per
+// table (synchronously, at the first call of a shape: make that call before
+// any stream capture) and kept with the host table that they copy.
+const int4* device_tri_table(const std::shared_ptr<const TriTable>& t) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  struct Entry { std::shared_ptr<const TriTable> host; int4* dev; };
+  static std::mutex mu;
+  static std::map<const TriTable*, Entry> cache[kMaxDevices];
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache[dev].find(t.get());
+  if (it != cache[dev].end()) return it->second.dev;
+  const std::vector<int4> image = t->device_image();
+  const size_t bytes = image.size() * sizeof(int4);
+  void* ptr = nullptr;
+  if (bytes == 0 || cudaMalloc(&ptr, bytes) != cudaSuccess) return nullptr;
+  if (cudaMemcpy(ptr, image.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(ptr);
+    return nullptr;
+  }
+  cache[dev].emplace(t.get(), Entry{t, static_cast<int4*>(ptr)});
+  return static_cast<int4*>(ptr);
+}
+
+// Bytes of caller workspace the triangular unit table takes when it must
+// live there (allocation-free calls): 0 for other plans.
+int64_t tri_gate_table_bytes(const b2g_gemm_desc* d, const b2g_gemm_plan& pl) {
+  if (d->op == B2G_OP_GEMM || d->precision == B2G_PREC_3XTF32 || pl.tri_diag) return 0;
+  const auto t = cached_tri_table(d, pl.block_m, pl.block_n, pl.tiles_m, pl.tiles_n,
+                                  pl.grid / pl.cluster_ctas, pl.tma_store);
+  return round_up(static_cast<int64_t>(t->units.size() + t->split_tiles.size()) * sizeof(int4),
+                  256);
+}
+
+// table_in_workspace: the triangular unit table is copied into the
+// workspace on every call (allocation-free callers) instead of the
+// per-device cache.
 static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* workspace,
-                       int* err_word, cudaStream_t stream, const float* row_bias = nullptr) {
+                       int* err_word, cudaStream_t stream, const float* row_bias = nullptr,
+                       bool table_in_workspace = false) {
   const float* a = d->a;
   const float* b = d->b;
   int64_t lda = d->lda, ldb = d->ldb, sa = d->stride_a, sb = d->stride_b;
@@ -1017,6 +1092,30 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
       return B2G_ERR_LAUNCH;
   }
 
+  // Triangular TF32 through the gated transform warps: the unit table from
+  // the per-device cache (or copied into the workspace), split tiles
+  // cleared in the kernel through tile flags.
+  const bool tri_gate = d->op != B2G_OP_GEMM && d->precision != B2G_PREC_3XTF32 && !pl.tri_diag;
+  std::shared_ptr<const TriTable> gate_table;
+  if (tri_gate) {
+    gate_table = cached_tri_table(d, pl.block_m, pl.block_n, pl.tiles_m, pl.tiles_n,
+                                  pl.grid / pl.cluster_ctas, pl.tma_store);
+    if (table_in_workspace) {
+      // The image is staged by the runtime before the call returns (pageable
+      // source), so the local vector may go out of scope.
+      const std::vector<int4> image = gate_table->device_image();
+      const int64_t tbytes = static_cast<int64_t>(image.size()) * sizeof(int4);
+      table = reinterpret_cast<int4*>(ws);
+      if (cudaMemcpyAsync(table, image.data(), tbytes, cudaMemcpyHostToDevice, stream) !=
+          cudaSuccess)
+        return B2G_ERR_LAUNCH;
+      ws += round_up(tbytes, 256);
+    } else {
+      table = const_cast<int4*>(device_tri_table(gate_table));
+      if (!table) return B2G_ERR_LAUNCH;
+    }
+  }
+
   EngineParams p;
   std::memset(&p, 0, sizeof(p));
   p.M = static_cast<int>(d->m);
@@ -1050,6 +1149,12 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.tri_sorted = (p.tri != kTriNone && pl.block_m == pl.block_n) ? 1 : 0;
   p.tri_diag = pl.tri_diag;
   p.unit_table = table;
+  p.xf_gate = tri_gate ? 1 : 0;
+  if (tri_gate && !gate_table->split_tiles.empty()) {
+    if (!tile_flag_region(&p.tile_flags, &p.epoch)) return B2G_ERR_LAUNCH;
+    p.split_tiles = table + gate_table->units.size();
+    p.n_split = static_cast<int>(gate_table->split_tiles.size());
+  }
   p.diag_oob_row = static_cast<int>(d->m);
   p.row_bias = row_bias;
   p.err = err_word;
@@ -1463,7 +1568,10 @@ extern "C" int b2g_gemm_noalloc(const b2g_gemm_desc* d, b2g_stream_t stream_hand
   rc = b2g_gemm_plan_for(d, st->num_sms, &pl);
   if (rc != B2G_OK) return rc;
   if (pl.workspace_bytes > B2G_NOALLOC_SCRATCH_BYTES) return B2G_ERR_SCRATCH_LIMIT;
-  return run_planned(d, pl, st->scratch, st->err, static_cast<cudaStream_t>(stream_handle));
+  if (pl.workspace_bytes + tri_gate_table_bytes(d, pl) > B2G_NOALLOC_SCRATCH_BYTES)
+    return B2G_ERR_SCRATCH_LIMIT;
+  return run_planned(d, pl, st->scratch, st->err, static_cast<cudaStream_t>(stream_handle),
+                     nullptr, true);
 }
 
 extern "C" int b2g_noalloc_read_error(int device, int32_t* code) {

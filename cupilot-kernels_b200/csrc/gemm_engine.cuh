@@ -89,7 +89,49 @@ struct EngineParams {
   // 7 tile flag seen (split-K), 8.. epilogue warp 0's chunk groups of its
   // last unit: TMEM data in registers, store issued (pairs of stamps).
   unsigned long long* trace;
+  // Triangular unit tables with split tiles: their (tm, tn) in .x / .y of
+  // n_split entries.  Every CTA (pair) first zeroes its share of them (tile
+  // j by cluster j % clusters) and stamps tile_flags slot j, before it
+  // takes any unit; the K pieces of a split tile then wait for that flag
+  // and reduce-add.  No wait depends on the order in which units run.
+  const int4* split_tiles;
+  int n_split;
+  // XF variants on triangular ops: 1 = only K blocks that the diagonal
+  // crosses (partly masked operand boxes) go through the transform warps;
+  // wholly masked boxes are loaded as TMA zero fill from outside the
+  // operand, the rest go straight to the MMA.  0 = every stage is
+  // transformed (3xTF32 split).
+  int xf_gate;
 };
+
+// Triangular masking of one operand box, for one CTA: 0 nothing masked,
+// 1 partly masked (the diagonal crosses the box), 2 wholly masked.
+// A: rows [m0, m0 + 128) x K block [k0, k0 + 32); upper zeroes k < i,
+// lower k > i (kernels/14_...:74-75, kernels/15_... assumes the same).
+__host__ __device__ inline int tri_mask_a(int tri, int m0, int k0) {
+  if (tri == kTriUpper) {
+    if (k0 + kBlockK - 1 < m0) return 2;
+    return k0 >= m0 + kBlockM - 1 ? 0 : 1;
+  }
+  if (tri == kTriLower) {
+    if (k0 > m0 + kBlockM - 1) return 2;
+    return k0 + kBlockK - 1 <= m0 ? 0 : 1;
+  }
+  return 0;
+}
+// B: K block [k0, k0 + 32) x columns [n0, n0 + cols); upper zeroes k > j,
+// lower k < j.
+__host__ __device__ inline int tri_mask_b(int tri, int n0, int cols, int k0) {
+  if (tri == kTriUpper) {
+    if (k0 > n0 + cols - 1) return 2;
+    return k0 + kBlockK - 1 <= n0 ? 0 : 1;
+  }
+  if (tri == kTriLower) {
+    if (k0 + kBlockK - 1 < n0) return 2;
+    return k0 >= n0 + cols - 1 ? 0 : 1;
+  }
+  return 0;
+}
 
 constexpr int kFlagSlots = 16;     // epilogue warps per tile (8 per CTA, a pair)
 
@@ -124,10 +166,12 @@ struct WorkUnit {
   int b, tm, tn, kb_lo, kb_hi;
   int accumulate;   // reduce-add into C (a K piece of a split tile)
   int skip;         // padding entry of a unit table: no work, no output
+  int flag;         // split tile: its slot in EngineParams::tile_flags, else -1
+  int first;        // the K piece that clears the tile before any piece adds
 };
 
-// Unit-table flags (bits 24.. of .w).
-enum : int { kUnitAccumulate = 1, kUnitSkip = 2 };
+// Unit-table entries: {tm | (flag slot + 1) << 16, tn, kb_lo, kb_hi | flags << 24}.
+enum : int { kUnitAccumulate = 1, kUnitSkip = 2, kUnitFirst = 4 };
 
 // Map a linear work-unit index to (batch, tile, K range).  Tiles are
 // rasterised in groups of group_m tile-rows so CTAs that run together share
@@ -170,6 +214,8 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
   WorkUnit u;
   u.accumulate = 0;
   u.skip = 0;
+  u.flag = -1;
+  u.first = 0;
   if (p.unit_table != nullptr) {
 #ifdef __CUDA_ARCH__
     const int4 e = __ldg(p.unit_table + w);
@@ -177,12 +223,14 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
     const int4 e = p.unit_table[w];
 #endif
     u.b = 0;
-    u.tm = e.x;
+    u.tm = e.x & 0xFFFF;
+    u.flag = (e.x >> 16) - 1;
     u.tn = e.y;
     u.kb_lo = e.z;
     u.kb_hi = e.w & 0xFFFFFF;
     u.accumulate = (e.w >> 24) & kUnitAccumulate;
     u.skip = ((e.w >> 24) & kUnitSkip) ? 1 : 0;
+    u.first = ((e.w >> 24) & kUnitFirst) ? 1 : 0;
     return u;
   }
   const int split = static_cast<int>(w % p.splits);
@@ -224,6 +272,10 @@ __host__ __device__ inline WorkUnit decode_unit(const EngineParams& p, long long
   if (hi < lo) hi = lo;
   u.kb_lo = lo;
   u.kb_hi = hi;
+  if (p.tile_flags != nullptr) {   // split-K: every piece of a tile shares its flags
+    u.flag = static_cast<int>(t);
+    u.first = split == 0;
+  }
   return u;
 }
 
@@ -554,6 +606,20 @@ __global__ void __launch_bounds__(
   units.unit0 = unit0;
   units.step = unit_step;
   units.dyn = p.sched != nullptr;
+  // Does stage (u, kb) go through the transform warps?  Every stage of an XF
+  // variant unless xf_gate; then only the K blocks that the diagonal crosses
+  // for either CTA of the pair (both CTAs decide alike).
+  auto gated = [&](const WorkUnit& u, int kb) -> bool {
+    if (!XF) return false;
+    if (X3 || !p.xf_gate) return true;
+    const int k0 = kb * kBlockK;
+#pragma unroll
+    for (int r = 0; r < Cfg::kCtas; ++r) {
+      if (tri_mask_a(p.tri, u.tm * Cfg::kUnitM + r * kBlockM, k0) == 1) return true;
+      if (tri_mask_b(p.tri, u.tn * BN + r * Cfg::kSubCols, Cfg::kBnCta, k0) == 1) return true;
+    }
+    return false;
+  };
 
   unsigned long long* trace = p.trace ? p.trace + static_cast<size_t>(blockIdx.x) * 16 : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = ptx::globaltimer_ns();
@@ -643,26 +709,41 @@ __global__ void __launch_bounds__(
             break;
           }
           // Each CTA's loads complete on its own barrier when transform warps
-          // must see them; otherwise a pair's loads complete on the leader's.
-          if (!PAIR || XF)
+          // must see them; otherwise a pair's loads complete on the leader's
+          // (and, in an XF pair, the other CTA arrives on its own barrier so
+          // that its phases stay in step with the leader's).
+          const bool xg = gated(u, kb);
+          const bool pair_load = PAIR && !xg;
+          if (!pair_load)
             ptx::mbar_arrive_expect_tx(&full[s], Cfg::kStageTx);
           else if (leader)
             ptx::mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageTx);
+          else if (XF)
+            ptx::mbar_arrive(&full[s]);
           uint8_t* sa = smem + Cfg::kOffA + s * Cfg::kABytes;
           uint8_t* sb = smem + Cfg::kOffB + s * Cfg::kBBytes;
           const int k0 = kb * kBlockK;
+          // Gated triangular stages: a wholly masked box of this CTA is read
+          // from a K coordinate before the operand (TMA writes zeros, no
+          // memory traffic); a partly masked one is loaded and masked by the
+          // transform warps.
+          int ka = k0, kbb = k0;
+          if (XF && !X3 && p.xf_gate) {
+            if (tri_mask_a(p.tri, m_cta, k0) == 2) ka = -kBlockK;
+            if (tri_mask_b(p.tri, n_cta, Cfg::kBnCta, k0) == 2) kbb = -kBlockK;
+          }
           auto load = [&](void* dst, const CUtensorMap* map, int c0, int c1, int c2) {
-            if (PAIR && !XF)
+            if (pair_load)
               ptx::tma_load_3d_pair(dst, map, full_leader + s * 8, c0, c1, c2);
             else
               ptx::tma_load_3d(dst, map, &full[s], c0, c1, c2);
           };
           // MN-major operand as {32, K, group, batch}: one box of all groups.
-          auto load_grouped = [&](void* dst, const CUtensorMap* map, int g0, int c3) {
-            if (PAIR && !XF)
-              ptx::tma_load_4d_pair(dst, map, full_leader + s * 8, 0, k0, g0, c3);
+          auto load_grouped = [&](void* dst, const CUtensorMap* map, int kc, int g0, int c3) {
+            if (pair_load)
+              ptx::tma_load_4d_pair(dst, map, full_leader + s * 8, 0, kc, g0, c3);
             else
-              ptx::tma_load_4d(dst, map, &full[s], 0, k0, g0, c3);
+              ptx::tma_load_4d(dst, map, &full[s], 0, kc, g0, c3);
           };
           // Triangular operands through diagonal-block copies: a K block that
           // crosses this CTA's diagonal block comes from the masked copy, one
@@ -686,7 +767,7 @@ __global__ void __launch_bounds__(
               if (k0 < c0 + Cfg::kSubCols) y = k0 >= c0 ? k0 : -kBlockK;
             }
             if (y != -1) {
-              if (PAIR && !XF)
+              if (pair_load)
                 ptx::tma_load_4d_pair(sb, &map_bd, full_leader + s * 8, 0, y, 0, 0);
               else
                 ptx::tma_load_4d(sb, &map_bd, &full[s], 0, y, 0, 0);
@@ -701,7 +782,7 @@ __global__ void __launch_bounds__(
             if (!A_MN) {
               load(sal, &map_ad, k0, m_cta, ab);
             } else if (p.a_grouped) {
-              load_grouped(sal, &map_ad, m_cta / 32, ab);
+              load_grouped(sal, &map_ad, k0, m_cta / 32, ab);
             } else {
 #pragma unroll
               for (int j = 0; j < kBlockM / 32; ++j)
@@ -714,7 +795,7 @@ __global__ void __launch_bounds__(
               if (!B_MN) {
                 load(sblj, &map_bd, k0, nj, bb);
               } else if (p.b_grouped) {
-                load_grouped(sblj, &map_bd, nj / 32, bb);
+                load_grouped(sblj, &map_bd, k0, nj / 32, bb);
               } else {
 #pragma unroll
                 for (int g = 0; g < Cfg::kSubCols / 32; ++g)
@@ -724,26 +805,26 @@ __global__ void __launch_bounds__(
           }
           if (a_done) {
           } else if (!A_MN) {
-            load(sa, &map_a, k0, m_cta, ab);
+            load(sa, &map_a, ka, m_cta, ab);
           } else if (p.a_grouped) {
-            load_grouped(sa, &map_a, m_cta / 32, ab);
+            load_grouped(sa, &map_a, ka, m_cta / 32, ab);
           } else {
 #pragma unroll
             for (int j = 0; j < kBlockM / 32; ++j)
-              load(sa + j * kBlockK * kSwRowBytes, &map_a, m_cta + 32 * j, k0, ab);
+              load(sa + j * kBlockK * kSwRowBytes, &map_a, m_cta + 32 * j, ka, ab);
           }
 #pragma unroll
           for (int j = 0; j < Cfg::kNSub && !b_done; ++j) {
             uint8_t* sbj = sb + j * Cfg::kBSubBytes;
             const int nj = n_cta + j * Cfg::kMmaN;
             if (!B_MN) {
-              load(sbj, &map_b, k0, nj, bb);
+              load(sbj, &map_b, kbb, nj, bb);
             } else if (p.b_grouped) {
-              load_grouped(sbj, &map_b, nj / 32, bb);
+              load_grouped(sbj, &map_b, kbb, nj / 32, bb);
             } else {
 #pragma unroll
               for (int g = 0; g < Cfg::kSubCols / 32; ++g)
-                load(sbj + g * kBlockK * kSwRowBytes, &map_b, nj + 32 * g, k0, bb);
+                load(sbj + g * kBlockK * kSwRowBytes, &map_b, nj + 32 * g, kbb, bb);
             }
           }
         }
@@ -786,6 +867,7 @@ __global__ void __launch_bounds__(
       constexpr uint32_t a_kstep = A_MN ? 8 * kSwRowBytes : 8 * 4;   // bytes per K=8 step
       constexpr uint32_t b_kstep = B_MN ? 8 * kSwRowBytes : 8 * 4;
       uint32_t it = 0, tl = 0;
+      uint32_t ready_par = 0;   // bit s: phase parity of ready[s] (counts gated uses only)
       bool ok = true;
       for (uint32_t ui = 0; ok; ++ui) {
         long long w;
@@ -808,12 +890,15 @@ __global__ void __launch_bounds__(
         for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
-          uint64_t* gate = XF ? &ready[s] : &full[s];
-          if (!ptx::mbar_wait(gate, ph, abort_flag, p.wait_limit_ns)) {
-            record_error(p.err, abort_flag, XF ? kErrWaitReady : kErrWaitFull);
+          const bool xg = gated(u, kb);
+          uint64_t* gate = xg ? &ready[s] : &full[s];
+          const uint32_t gph = xg ? ((ready_par >> s) & 1u) : ph;
+          if (!ptx::mbar_wait(gate, gph, abort_flag, p.wait_limit_ns)) {
+            record_error(p.err, abort_flag, xg ? kErrWaitReady : kErrWaitFull);
             ok = false;
             break;
           }
+          if (xg) ready_par ^= 1u << s;
           if (trace && it == 0) trace[2] = ptx::globaltimer_ns();
           ptx::tc_fence_after();
           const uint32_t sa = ptx::smem_addr(smem + Cfg::kOffA + s * Cfg::kABytes);
@@ -886,6 +971,39 @@ __global__ void __launch_bounds__(
     const uint32_t tmem_empty_leader =
         PAIR ? ptx::mapa_shared(ptx::smem_addr(tmem_empty), 0) : 0u;
     uint32_t tl = 0, seq = 0;
+    // Zero this warp's chunks of a tile region (TMA zero boxes), wait until
+    // the stores are complete, then stamp `flag` with the launch's epoch.
+    auto zero_and_flag = [&](int row0, int n0, int b, unsigned* flag) {
+      if (row0 < p.M) {
+        if (lane == 0) ptx::bulk_wait_read<0>();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(stg + lane * 32 + j * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          for (int ch = half; ch * 32 < BN && n0 + ch * 32 < p.N; ch += kParts)
+            ptx::tma_store_3d(&map_c, stg, n0 + ch * 32, row0, b);
+          ptx::bulk_commit();
+          ptx::bulk_wait_all();
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        ptx::fence_proxy_async_global();
+        __threadfence();
+        ptx::st_release_gpu(flag, p.epoch);
+      }
+    };
+    if (p.split_tiles != nullptr && p.tile_flags != nullptr && p.tma_store) {
+      const int cluster = static_cast<int>(unit0), clusters = static_cast<int>(unit_step);
+      for (int j = cluster; j < p.n_split; j += clusters) {
+        const int4 t = p.split_tiles[j];
+        zero_and_flag(t.x * Cfg::kUnitM + static_cast<int>(rank) * kBlockM + quad * 32, t.y * BN,
+                      0, p.tile_flags + j * kFlagSlots + static_cast<int>(rank) * Cfg::kEpiWarps + ew);
+      }
+    }
     for (uint32_t ui = 0;; ++ui) {
       long long w;
       if (!units.get(ui, w, abort_flag, p.wait_limit_ns)) {
@@ -936,34 +1054,12 @@ __global__ void __launch_bounds__(
         continue;
       }
       unsigned* tile_flag = nullptr;
-      if (p.tile_flags != nullptr) {
-        const int tile = (u.b * p.tiles_m + u.tm) * p.tiles_n + u.tn;
-        tile_flag = p.tile_flags + tile * kFlagSlots + static_cast<int>(rank) * Cfg::kEpiWarps + ew;
-        if (u.kb_lo == 0) {
-          // First K piece: zero this warp's chunks of the tile, let the
-          // stores complete, then publish them (before waiting for the MMA).
-          if (row0 < p.M) {
-            if (lane == 0) ptx::bulk_wait_read<0>();
-            __syncwarp();
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              *reinterpret_cast<float4*>(stg + lane * 32 + j * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
-            ptx::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              for (int ch = half; ch * 32 < BN && n0 + ch * 32 < p.N; ch += kParts)
-                ptx::tma_store_3d(&map_c, stg, n0 + ch * 32, row0, u.b);
-              ptx::bulk_commit();
-              ptx::bulk_wait_all();
-            }
-          }
-          __syncwarp();
-          if (lane == 0) {
-            ptx::fence_proxy_async_global();
-            __threadfence();
-            ptx::st_release_gpu(tile_flag, p.epoch);
-          }
-        }
+      if (p.tile_flags != nullptr && u.flag >= 0) {
+        tile_flag = p.tile_flags + u.flag * kFlagSlots + static_cast<int>(rank) * Cfg::kEpiWarps + ew;
+        // Split-K: the first K piece zeroes this warp's chunks of the tile
+        // and publishes them (before waiting for the MMA).  Split tiles of a
+        // unit table were zeroed before any unit (above).
+        if (u.first && p.split_tiles == nullptr) zero_and_flag(row0, n0, u.b, tile_flag);
       }
       const int buf = tl % Cfg::kAccBufs;
       const uint32_t uph = (tl / Cfg::kAccBufs) & 1;
@@ -973,7 +1069,7 @@ __global__ void __launch_bounds__(
       }
       if (trace && ew == 0 && lane == 0 && tl == 0) trace[4] = ptx::globaltimer_ns();
       ptx::tc_fence_after();
-      if (tile_flag != nullptr && u.kb_lo != 0 && row0 < p.M) {
+      if (tile_flag != nullptr && (!u.first || p.split_tiles != nullptr) && row0 < p.M) {
         // Later K piece: its reduce-adds land on chunks the first piece zeroes.
         int ok = 1;
         if (lane == 0) {
@@ -1109,19 +1205,26 @@ __global__ void __launch_bounds__(
       for (int kb = u.kb_lo; kb < u.kb_hi; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
+        // Every phase of full[s] is waited for, also for stages that go
+        // straight to the MMA: a parity wait that skipped a phase could
+        // return on the skipped phase's parity before this stage landed.
         if (!ptx::mbar_wait(&full[s], ph, abort_flag, p.wait_limit_ns)) {
           if (lane == 0) record_error(p.err, abort_flag, kErrWaitXform);
           ok = false;
           break;
         }
+        if (!gated(u, kb)) continue;       // straight to the MMA
         const int k0 = kb * kBlockK;
         int rule_a = 0, rule_b = 0;
-        if (p.tri == kTriUpper) {          // A: zero k < i ; B: zero k > j
-          if (k0 < m0 + kBlockM - 1) rule_a = 1;
-          if (k0 + kBlockK - 1 > n0) rule_b = 2;
-        } else if (p.tri == kTriLower) {   // A: zero k > i ; B: zero k < j
-          if (k0 + kBlockK - 1 > m0) rule_a = 2;
-          if (k0 < n0 + Cfg::kBnCta - 1) rule_b = 1;
+        const int up = p.tri == kTriUpper;   // rule 1: zero k < mn; rule 2: zero k > mn
+        if (p.xf_gate && !X3) {
+          // Only partly masked boxes need work; wholly masked ones were
+          // loaded as zeros.
+          if (tri_mask_a(p.tri, m0, k0) == 1) rule_a = up ? 1 : 2;
+          if (tri_mask_b(p.tri, n0, Cfg::kBnCta, k0) == 1) rule_b = up ? 2 : 1;
+        } else if (p.tri != kTriNone) {
+          if (tri_mask_a(p.tri, m0, k0) != 0) rule_a = up ? 1 : 2;
+          if (tri_mask_b(p.tri, n0, Cfg::kBnCta, k0) != 0) rule_b = up ? 2 : 1;
         }
         float* ta = reinterpret_cast<float*>(smem + Cfg::kOffA + s * Cfg::kABytes);
         float* tb = reinterpret_cast<float*>(smem + Cfg::kOffB + s * Cfg::kBBytes);

@@ -157,7 +157,9 @@ B2G_API int b2g_rowscale(const float* d, const float* b, float* out, int64_t row
  *     so 3xTF32 fits only while A and B together hold at most ~4 M elements;
  *   - every triangular call in TF32 on untransposed operands, aligned or
  *     not: masked copies of the diagonal blocks (2 * n * 128 floats) and the
- *     unit table (16 bytes per unit), so n is limited to about 16000.
+ *     unit table (16 bytes per unit), so n is limited to about 16000; on
+ *     transposed operands the unit table only (b2g_gemm keeps that one in a
+ *     device cache of its own instead of the caller's workspace).
  * A descriptor needing more than that returns B2G_ERR_SCRATCH_LIMIT before
  * any work is issued; b2g_gemm_workspace_bytes() tells how much it needs.
  *

@@ -108,13 +108,18 @@ def test_plan_large_k_splits(capi):
 
 
 def test_plan_triangular_never_splits(capi):
+    """Triangular TF32 products: CTA pairs, no split-K, one table row of units
+    per CTA pair.  Untransposed operands mask through diagonal-block copies
+    in workspace; transposed layouts mask inside the engine (gated transform
+    warps) and need no workspace (the unit table lives in a per-device
+    cache)."""
     p = _plan(capi, 256, 256, 256, op=capi.OP_TRI_UPPER)
     assert p.splits == 1 and p.cluster_ctas == 2 and p.tri_diag == 1
-    # diagonal-block copies of A and B (2 x 256 rows x 128 fp32) plus the unit table
     assert p.workspace_bytes >= 2 * 256 * 128 * 4
-    assert p.work_units % (p.grid // 2) == 0   # table rows of one entry per CTA pair
+    assert p.work_units % (p.grid // 2) == 0
     q = _plan(capi, 256, 256, 256, op=capi.OP_TRI_LOWER, trans_a=1)
-    assert q.tri_diag == 0 and q.cluster_ctas == 1
+    assert q.tri_diag == 0 and q.cluster_ctas == 2 and q.workspace_bytes == 0
+    assert q.work_units % (q.grid // 2) == 0
 
 
 def test_plan_irregular_stages_unaligned_operands(capi):

@@ -293,3 +293,65 @@ def test_split_k_clears_output_in_kernel(ops, m, n, k):
         assert torch.isfinite(C).all()
         _check(C, ref, "tf32")
     assert ops.read_device_error(torch.cuda.current_device()) == 0
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("pid", [14, 15])
+@pytest.mark.parametrize("n", [300, 1024, 4096])
+@pytest.mark.parametrize("views", ["ta", "tb", "tatb"])
+def test_triangular_transposed_views(ops, mode, pid, n, views):
+    """Triangular products on transposed operand views (A or B stored
+    transposed, read in place): the engine masks the K blocks that the
+    diagonal crosses in its transform warps and loads wholly masked boxes as
+    zero fill (TF32), or transforms every stage (3xTF32).  Unmasked N(0,1)
+    inputs: the operator masks them itself (kernels/14_...:74-75,84-85)."""
+    g = _gen(pid * 7 + n + len(views))
+    A, B = _randn(g, n, n), _randn(g, n, n)
+    Ad = A.t().contiguous().cuda().t() if "ta" in views else A.cuda()
+    Bd = B.t().contiguous().cuda().t() if "tb" in views else B.cuda()
+    with ops.precision(mode):
+        C = ops.OPERATORS[pid].forward(Ad, Bd)
+    _check(C, O.BY_PID[pid](A.numpy(), B.numpy()), mode)
+    masked = torch.tril(C, -1) if pid == 14 else torch.triu(C, 1)
+    assert torch.count_nonzero(masked).item() == 0
+    assert ops.read_device_error(torch.cuda.current_device()) == 0
+
+
+GATE_CHILD = r"""
+import importlib, json, sys, torch
+sys.path.insert(0, sys.argv[1])
+ops = importlib.import_module("cupilot-kernels_b200.ops")
+out = []
+for pid, n in ((14, 4096), (15, 4096), (14, 1536), (15, 2048)):
+    g = torch.Generator(device="cuda").manual_seed(pid + n)
+    A = torch.randn(n, n, generator=g, device="cuda")
+    B = torch.randn(n, n, generator=g, device="cuda")
+    tri = torch.triu if pid == 14 else torch.tril
+    ref = tri(tri(A).double() @ tri(B).double())
+    C = ops.OPERATORS[pid].forward(A, B)
+    masked = torch.tril(C, -1) if pid == 14 else torch.triu(C, 1)
+    out.append([float(((C.double() - ref).norm() / ref.norm()).item()),
+                int(torch.count_nonzero(masked).item())])
+print(json.dumps({"res": out, "code": ops.read_device_error(0)}))
+"""
+
+
+def test_triangular_gated_path_on_untransposed_operands():
+    """The in-engine masking (B2G_TRI_PATH=gate, a tuning knob) on the
+    untransposed configs, where it runs split tiles cleared in the kernel
+    and many units per CTA pair."""
+    import json
+    import os
+    import subprocess
+    import sys
+
+    from conftest import REPO
+
+    env = dict(os.environ, B2G_TUNING="1", B2G_TRI_PATH="gate")
+    r = subprocess.run([sys.executable, "-c", GATE_CHILD, str(REPO)], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert out["code"] == 0, out
+    for err, nz in out["res"]:
+        assert err <= 1e-2 and nz == 0, out
