@@ -45,6 +45,9 @@
 #ifndef B2G_PAIR256_EPIW
 #define B2G_PAIR256_EPIW 8     // epilogue warps of the CTA-pair 256-wide engine
 #endif
+#ifndef B2G_PAIR256_LONGK_EPIW
+#define B2G_PAIR256_LONGK_EPIW 4   // ... for units of >= 16 K blocks
+#endif
 
 namespace b2g {
 namespace {
@@ -1258,7 +1261,8 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
       // Long K loops: 4 epilogue warps drain a unit well inside the next
       // unit's mainloop and compete less with it (bmm 128 x 512x2048x1024:
       // +7 % in bursts, +2 % sustained under the power cap).
-      return launch_majors<256, B2G_PAIR256_STAGES, false, false, true, B2G_PAIR256_EPIG, 4>(
+      return launch_majors<256, B2G_PAIR256_STAGES, false, false, true, B2G_PAIR256_EPIG,
+                           B2G_PAIR256_LONGK_EPIW>(
           a_mn, b_mn, maps, p, grid, stream);
     if (pl.block_n == 256)
       return launch_majors<256, B2G_PAIR256_STAGES, false, false, true, B2G_PAIR256_EPIG,
