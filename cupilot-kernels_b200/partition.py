@@ -144,6 +144,34 @@ class Partitioner:
         dist.reduce(part, dst=root, op=dist.ReduceOp.SUM, group=self.group)
         return part if self.rank == root else None
 
+    def split_k_matmul_async(self, A_k: torch.Tensor, B_k: torch.Tensor,
+                             root: int = 0) -> Optional[torch.Tensor]:
+        """split_k_matmul with the cross-GPU sum taken off the caller's
+        stream: the GEMM runs on the current stream, the peer reduction on a
+        side stream behind it, so the next call's GEMM does not wait for this
+        call's sum.  The returned C (root) is complete only after `join()`,
+        which makes the current stream wait for every sum issued so far."""
+        if self.world == 1 or not A_k.is_cuda:
+            return self.split_k_matmul(A_k, B_k, root=root)
+        part = self._mm()(A_k, B_k)
+        red = self.peer_reducer(part.numel())
+        cur = torch.cuda.current_stream(part.device)
+        side = self.__dict__.get("_side")
+        if side is None:
+            side = torch.cuda.Stream(part.device)
+            self.__dict__["_side"] = side
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            red.reduce(part, part if self.rank == root else None, root)
+        part.record_stream(side)      # the allocator keeps it until the side stream is done
+        return part if self.rank == root else None
+
+    def join(self) -> None:
+        """Make the current stream wait for the sums split_k_matmul_async issued."""
+        side = self.__dict__.get("_side")
+        if side is not None:
+            torch.cuda.current_stream(side.device).wait_stream(side)
+
     def peer_reducer(self, elems: int, backend=None) -> "PeerReducer":
         """The mailbox set for partials of `elems` floats, created on first use
         (a collective call: every rank must reach it)."""

@@ -14,7 +14,9 @@
   GEMM in the same context is correct.
 * Two GPUs (skipped with fewer): torchrun with two ranks runs the large-K
   product split over K through Partitioner.split_k_matmul(method="peer"),
-  three calls in a row, checked on the root against a float64 product.
+  three calls in a row, then three pipelined calls (split_k_matmul_async:
+  the sums on a side stream behind the GEMMs) and a join, each result
+  checked on the root against a float64 product.
 """
 import json
 import os
@@ -120,6 +122,21 @@ for step in range(3):
         res.append(float(((C.double() - ref).norm() / ref.norm()).item()))
     else:
         assert C is None
+# Pipelined: three sums on the side stream behind three GEMMs, then join.
+outs, refs = [], []
+for step in range(3):
+    g = torch.Generator(device="cuda").manual_seed(200 + step)
+    A = torch.randn(m, k, generator=g, device="cuda")
+    B = torch.randn(k, n, generator=g, device="cuda")
+    k0, k1 = p.k_range(k)
+    outs.append(p.split_k_matmul_async(A[:, k0:k1].contiguous(), B[k0:k1].contiguous(), root=0))
+    refs.append((A, B))
+p.join()
+torch.cuda.synchronize()
+if p.rank == 0:
+    for C, (A, B) in zip(outs, refs):
+        ref = A.double() @ B.double()
+        res.append(float(((C.double() - ref).norm() / ref.norm()).item()))
 err_code = ops.read_device_error(torch.cuda.current_device())
 codes = [None] * p.world
 dist.all_gather_object(codes, err_code)
@@ -142,4 +159,4 @@ def test_peer_reduce_two_gpus(tmp_path):
     assert r.returncode == 0, r.stderr[-3000:]
     out = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
     assert out["codes"] == [0, 0], out
-    assert len(out["errs"]) == 3 and max(out["errs"]) <= 1e-2, out
+    assert len(out["errs"]) == 6 and max(out["errs"]) <= 1e-2, out
