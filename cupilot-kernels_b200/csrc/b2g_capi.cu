@@ -435,29 +435,50 @@ __global__ void __launch_bounds__(256) tri_prepare_kernel(
   }
 }
 
-// 3xTF32 pre-split: dst[b][r][c] = x - (x with its low 13 mantissa bits
-// cleared), x = src[b*sstride + r*sld + c]; the tensor core truncates the
-// original operand to its TF32 "hi" part itself.
-__global__ void __launch_bounds__(256) split_lo_kernel(const float* __restrict__ src,
-                                                       float* __restrict__ dst, int64_t rows,
-                                                       int64_t cols, int64_t sld, int64_t sstride,
-                                                       int64_t dld, int64_t dstride,
-                                                       int64_t batch) {
-  const int64_t total = batch * rows;
+// 3xTF32 pre-split of both operands in one launch (blockIdx.y: 0 = A,
+// 1 = B): dst[b][r][c] = x - (x with its low 13 mantissa bits cleared),
+// x = src[b*sstride + r*sld + c]; the tensor core truncates the original
+// operand to its TF32 "hi" part itself.  Sources are 16-byte aligned rows
+// (an operand with another pitch was staged first); each thread keeps four
+// 16-byte loads in flight.  Launched programmatically: the engine behind it
+// sets up meanwhile and waits for it before reading.
+struct SplitJob {
+  const float* src;
+  float* dst;
+  int64_t rows, cols, sld, sstride, dld, dstride, batch;
+};
+__global__ void __launch_bounds__(256) split_lo_kernel(const SplitJob ja, const SplitJob jb) {
+  ptx::griddep_launch_dependents();
+  ptx::griddep_wait();
+  const SplitJob& j = blockIdx.y == 0 ? ja : jb;
+  if (j.rows == 0) return;
+  constexpr int kIlp = 4;
+  auto lo = [](float x) { return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); };
+  const int64_t n4 = j.dld / 4;
+  const int64_t total = j.batch * j.rows;
   for (int64_t rr = blockIdx.x; rr < total; rr += gridDim.x) {
-    const int64_t b = rr / rows, r = rr - b * rows;
-    const float* s = src + b * sstride + r * sld;
-    float4* d = reinterpret_cast<float4*>(dst + b * dstride + r * dld);
-    // 16-byte destination rows (pitch a multiple of 4): float4 stores.
-    const int64_t n4 = dld / 4;
-    for (int64_t q = threadIdx.x; q < n4; q += blockDim.x) {
-      float e[4];
+    const int64_t b = rr / j.rows, r = rr - b * j.rows;
+    const float* s = j.src + b * j.sstride + r * j.sld;
+    float4* d = reinterpret_cast<float4*>(j.dst + b * j.dstride + r * j.dld);
+    for (int64_t q0 = threadIdx.x; q0 < n4; q0 += kIlp * blockDim.x) {
+      float4 v[kIlp];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float x = 4 * q + j < cols ? __ldg(s + 4 * q + j) : 0.f;
-        e[j] = x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+      for (int u = 0; u < kIlp; ++u) {
+        const int64_t q = q0 + static_cast<int64_t>(u) * blockDim.x;
+        if (q < n4 && 4 * q + 3 < j.cols) {
+          v[u] = __ldg(reinterpret_cast<const float4*>(s) + q);
+        } else if (q < n4) {
+          float e[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) e[t] = 4 * q + t < j.cols ? __ldg(s + 4 * q + t) : 0.f;
+          v[u] = make_float4(e[0], e[1], e[2], e[3]);
+        }
       }
-      d[q] = make_float4(e[0], e[1], e[2], e[3]);
+#pragma unroll
+      for (int u = 0; u < kIlp; ++u) {
+        const int64_t q = q0 + static_cast<int64_t>(u) * blockDim.x;
+        if (q < n4) d[q] = make_float4(lo(v[u].x), lo(v[u].y), lo(v[u].z), lo(v[u].w));
+      }
     }
   }
 }
@@ -1014,7 +1035,7 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     ws += g.bytes;
   }
 
-  // 3xTF32 pre-split: lo copies of A and B at a 16-byte pitch.
+  // 3xTF32 pre-split: lo copies of A and B at a 16-byte pitch, one launch.
   const float* alo = nullptr;
   const float* blo = nullptr;
   int64_t ldalo = 0, ldblo = 0, salo = 0, sblo = 0;
@@ -1023,14 +1044,23 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
                           d->trans_a ? 32 : 4);
     float* da = reinterpret_cast<float*>(ws);
     ws += ga.bytes;
-    split_lo_kernel<<<static_cast<int>(std::min<int64_t>(ga.rows * ga.nbatch, 65535)), 256, 0,
-                      stream>>>(a, da, ga.rows, ga.cols, lda, sa, ga.pitch, ga.bstride, ga.nbatch);
     Stage gb = stage_geom(d->trans_b ? d->n : d->k, d->trans_b ? d->k : d->n, b_batch,
                           d->trans_b ? 4 : 32);
     float* db = reinterpret_cast<float*>(ws);
     ws += gb.bytes;
-    split_lo_kernel<<<static_cast<int>(std::min<int64_t>(gb.rows * gb.nbatch, 65535)), 256, 0,
-                      stream>>>(b, db, gb.rows, gb.cols, ldb, sb, gb.pitch, gb.bstride, gb.nbatch);
+    const SplitJob ja{a, da, ga.rows, ga.cols, lda, sa, ga.pitch, ga.bstride, ga.nbatch};
+    const SplitJob jb{b, db, gb.rows, gb.cols, ldb, sb, gb.pitch, gb.bstride, gb.nbatch};
+    const int64_t rows = std::max(ga.rows * ga.nbatch, gb.rows * gb.nbatch);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(rows, 65535)), 2, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = B2G_PDL ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, split_lo_kernel, ja, jb) != cudaSuccess) return B2G_ERR_LAUNCH;
     alo = da;
     blo = db;
     ldalo = ga.pitch;
