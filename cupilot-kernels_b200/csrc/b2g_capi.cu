@@ -172,7 +172,7 @@ bool tri_epiw8() {
   return tuning_mode() ? read() : once;
 }
 
-// B2G_TRACE_PTR=<device address of 16 u64 per CTA> (tuning mode only): the
+// B2G_TRACE_PTR=<device address of 64 u64 per CTA> (tuning mode only): the
 // engine writes its per-CTA phase stamps there (EngineParams::trace).
 unsigned long long* trace_pointer() {
   if (!tuning_mode()) return nullptr;

@@ -82,12 +82,15 @@ struct EngineParams {
   unsigned* tile_flags;
   unsigned epoch;
   int* err;
-  // Tuning aid (null in normal use): per CTA, 16 globaltimer stamps at
-  // trace[cta * 16 + i]: 0 entry, 1 after the grid-dependency wait, 2 first
+  // Tuning aid (null in normal use): per CTA, 64 words at trace[cta * 64]:
+  // globaltimer stamps 0 entry, 1 after the grid-dependency wait, 2 first
   // operand stage landed (MMA warp), 3 last MMA issued, 4 first accumulator
   // ready (epilogue warp 0), 5 last store issued (epilogue warp 0), 6 exit,
   // 7 tile flag seen (split-K), 8.. epilogue warp 0's chunk groups of its
-  // last unit: TMEM data in registers, store issued (pairs of stamps).
+  // last unit: TMEM data in registers, store issued (pairs of stamps);
+  // MMA warp totals 16 ns spent waiting for operand stages, 17 ns waiting
+  // for a free accumulator buffer, 18 units; 20 + 2u / 21 + 2u: unit u's
+  // first operand stage landed / last MMA issued (u < 20).
   unsigned long long* trace;
   // Triangular unit tables with split tiles: their (tm, tn) in .x / .y of
   // n_split entries.  Every CTA (pair) first zeroes its share of them (tile
@@ -621,7 +624,7 @@ __global__ void __launch_bounds__(
     return false;
   };
 
-  unsigned long long* trace = p.trace ? p.trace + static_cast<size_t>(blockIdx.x) * 16 : nullptr;
+  unsigned long long* trace = p.trace ? p.trace + static_cast<size_t>(blockIdx.x) * 64 : nullptr;
   if (trace && threadIdx.x == 0) trace[0] = ptx::globaltimer_ns();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -880,10 +883,12 @@ __global__ void __launch_bounds__(
         if (u.kb_lo >= u.kb_hi) continue;
         const int buf = tl % Cfg::kAccBufs;
         const uint32_t uph = (tl / Cfg::kAccBufs) & 1;
+        const uint64_t te0 = trace ? ptx::globaltimer_ns() : 0;
         if (!ptx::mbar_wait(&tmem_empty[buf], uph ^ 1, abort_flag, p.wait_limit_ns)) {
           record_error(p.err, abort_flag, kErrWaitTmemEmpty);
           break;
         }
+        if (trace) trace[17] += ptx::globaltimer_ns() - te0;
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         uint32_t acc = 0;
@@ -893,13 +898,19 @@ __global__ void __launch_bounds__(
           const bool xg = gated(u, kb);
           uint64_t* gate = xg ? &ready[s] : &full[s];
           const uint32_t gph = xg ? ((ready_par >> s) & 1u) : ph;
+          const uint64_t tf0 = trace ? ptx::globaltimer_ns() : 0;
           if (!ptx::mbar_wait(gate, gph, abort_flag, p.wait_limit_ns)) {
             record_error(p.err, abort_flag, xg ? kErrWaitReady : kErrWaitFull);
             ok = false;
             break;
           }
           if (xg) ready_par ^= 1u << s;
-          if (trace && it == 0) trace[2] = ptx::globaltimer_ns();
+          if (trace) {
+            const uint64_t tf1 = ptx::globaltimer_ns();
+            trace[16] += tf1 - tf0;
+            if (it == 0) trace[2] = tf1;
+            if (kb == u.kb_lo && tl < 20) trace[20 + 2 * tl] = tf1;
+          }
           ptx::tc_fence_after();
           const uint32_t sa = ptx::smem_addr(smem + Cfg::kOffA + s * Cfg::kABytes);
           const uint32_t sb = ptx::smem_addr(smem + Cfg::kOffB + s * Cfg::kBBytes);
@@ -941,7 +952,11 @@ __global__ void __launch_bounds__(
             ptx::mma_commit(&empty[s]);
         }
         if (!ok) break;
-        if (trace) trace[3] = ptx::globaltimer_ns();
+        if (trace) {
+          trace[3] = ptx::globaltimer_ns();
+          if (tl < 20) trace[21 + 2 * tl] = trace[3];
+          trace[18] += 1;
+        }
         if (!p.inject_stall) {
           if (PAIR)
             ptx::mma_commit_pair(&tmem_full[buf], 0x3);
