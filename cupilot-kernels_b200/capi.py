@@ -214,6 +214,14 @@ def splitk_peer_reduce(partial: int, out: int, elems: int, mailboxes, rank: int,
                                         epoch, C.c_void_p(stream))
 
 
+def torch_splitk_peer_reduce(t, mailboxes, rank, root, epoch):
+    """b2g_splitk_peer_reduce through the Torch extension (no ctypes
+    conversion per call): t is the root's output or another rank's partial."""
+    from . import native
+
+    native().splitk_peer_reduce(t, list(mailboxes), rank, root, epoch)
+
+
 def read_device_error(device: int = 0) -> int:
     code = C.c_int32(0)
     rc = lib().b2g_read_device_error(device, C.byref(code))

@@ -166,16 +166,22 @@ __global__ void __launch_bounds__(kThreads) peer_reduce_kernel(float* __restrict
   const int64_t i = c * kChunk + static_cast<int64_t>(t) * 4;
   if (i + 4 <= elems) {
     float4 acc = *reinterpret_cast<const float4*>(out + i);
-    for (int r = 0; r < world; ++r) {
-      if (r == root) continue;
-      // L2 loads: the landed data was written by another GPU since this
-      // SM may last have cached the slot.
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(slot + r * stride + i));
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
-    }
+    // Every rank's landed chunk is loaded before any is added (the loads
+    // overlap), then summed in rank order.  L2 loads: the landed data was
+    // written by another GPU since this SM may last have cached the slot.
+    float4 v[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world && r != root)
+        v[r] = __ldcg(reinterpret_cast<const float4*>(slot + r * stride + i));
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < world && r != root) {
+        acc.x += v[r].x;
+        acc.y += v[r].y;
+        acc.z += v[r].z;
+        acc.w += v[r].w;
+      }
     *reinterpret_cast<float4*>(out + i) = acc;
   } else {
     for (int64_t j = i; j < elems; ++j) {

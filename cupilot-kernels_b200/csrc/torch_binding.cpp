@@ -400,6 +400,27 @@ void set_thread_precision(int64_t p) {
 }
 int64_t get_thread_precision() { return t_precision; }
 
+// One epoch of the cross-GPU K-split sum on the current stream (the
+// partitioner's per-step call; the same as b2g_splitk_peer_reduce through
+// ctypes, without the per-call conversion cost).  t: the root's output
+// (holding its own partial) or another rank's partial.
+void splitk_peer_reduce(at::Tensor t, std::vector<int64_t> mailboxes, int64_t rank, int64_t root,
+                        int64_t epoch) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous(),
+              "peer reduce needs a contiguous CUDA float32 tensor");
+  std::vector<void*> boxes(mailboxes.size());
+  for (size_t r = 0; r < mailboxes.size(); ++r) boxes[r] = reinterpret_cast<void*>(mailboxes[r]);
+  const c10::cuda::CUDAGuard guard(t.device());
+  auto stream = at::cuda::getCurrentCUDAStream(t.device().index());
+  float* p = t.data_ptr<float>();
+  const bool is_root = rank == root;
+  check_status(b2g_splitk_peer_reduce(is_root ? nullptr : p, is_root ? p : nullptr, t.numel(),
+                                      boxes.data(), static_cast<int>(boxes.size()),
+                                      static_cast<int>(rank), static_cast<int>(root), epoch,
+                                      stream.stream()),
+               "b2g_splitk_peer_reduce");
+}
+
 int64_t read_device_error(int64_t device) {
   int32_t code = 0;
   check_status(b2g_read_device_error(static_cast<int>(device), &code), "b2g_read_device_error");
@@ -440,4 +461,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_thread_precision", &set_thread_precision);
   m.def("get_thread_precision", &get_thread_precision);
   m.def("read_device_error", &read_device_error);
+  m.def("splitk_peer_reduce", &splitk_peer_reduce, "one epoch of the cross-GPU K-split sum");
 }

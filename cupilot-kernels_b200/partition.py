@@ -219,6 +219,10 @@ class PeerReducer:
         t = out if is_root else partial
         if t is None or t.numel() != self.elems or not t.is_contiguous():
             raise ValueError("peer reduce needs a contiguous tensor of the mailbox's size")
+        fast = getattr(self.backend, "torch_splitk_peer_reduce", None)
+        if fast is not None and t.is_cuda:
+            fast(t, self.mailboxes, self.part.rank, root, self.epoch)   # raises on failure
+            return
         stream = torch.cuda.current_stream(t.device).cuda_stream if t.is_cuda else 0
         rc = self.backend.splitk_peer_reduce(0 if is_root else t.data_ptr(),
                                              t.data_ptr() if is_root else 0, self.elems,
