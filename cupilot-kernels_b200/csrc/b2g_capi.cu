@@ -180,6 +180,16 @@ unsigned long long* trace_pointer() {
   return (e && *e) ? reinterpret_cast<unsigned long long*>(std::strtoull(e, nullptr, 0)) : nullptr;
 }
 
+// B2G_EARLY_DRAW=0 turns off drawing the next dynamic unit one unit ahead
+// (EngineParams::early_draw; a tuning knob, read once per process).
+bool early_draw_on() {
+  static const bool on = [] {
+    const char* e = std::getenv("B2G_EARLY_DRAW");
+    return !(e && *e == '0');
+  }();
+  return on;
+}
+
 int take_injected_stall() {
   static std::atomic<int> armed{-1};
   int v = armed.load();
@@ -362,27 +372,20 @@ struct TableParam {
   int split_off;   // word offset of the split-tile list (int2 pairs)
   int4 w[kTableParamWords];
 };
-__global__ void __launch_bounds__(256) tri_prepare_kernel(
+// The pre-pass's work once the table is in place.  Split tile i is
+// split4[i].{x,y} when split4 is set (the per-device table cache's image),
+// else split2[i].
+__device__ __forceinline__ void tri_prepare_body(
     const float* __restrict__ a, int64_t lda, const float* __restrict__ b, int64_t ldb, int64_t n,
     int upper, float* __restrict__ adiag, float* __restrict__ bdiag, float* __restrict__ c,
-    int64_t ldc, const int2* __restrict__ split_tiles, int n_split, int block_m, int block_n,
-    int4* __restrict__ table_dst, const __grid_constant__ TableParam tp) {
+    int64_t ldc, const int2* __restrict__ split2, const int4* __restrict__ split4, int n_split,
+    int block_m, int block_n) {
   constexpr int kSlices = kTriDiagBlock / kTriDiagRows;
-  // Launched with programmatic stream serialization: let the engine launch
-  // (it waits for this grid before reading), and wait for the previous
-  // kernel, which may still read the workspace this pass rewrites.
-  ptx::griddep_launch_dependents();
-  ptx::griddep_wait();
-  if (tp.words > 0) {
-    if (blockIdx.y == 1)   // B's blocks also copy the table (grid-stride over x)
-      for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tp.words; i += gridDim.x * blockDim.x)
-        table_dst[i] = tp.w[i];
-    split_tiles = reinterpret_cast<const int2*>(tp.w + tp.split_off);
-  }
   if (blockIdx.y == 2) {
     const int slices = (block_m + kTriDiagRows - 1) / kTriDiagRows;
     if (static_cast<int>(blockIdx.x) >= n_split * slices) return;
-    const int2 t = split_tiles[blockIdx.x / slices];
+    const int si = blockIdx.x / slices;
+    const int2 t = split4 ? make_int2(split4[si].x, split4[si].y) : split2[si];
     const int r0 = (blockIdx.x % slices) * kTriDiagRows;
     const int64_t col_base = static_cast<int64_t>(t.y) * block_n;
     if ((reinterpret_cast<uintptr_t>(c) % 16) == 0 && ldc % 4 == 0 && col_base + block_n <= n) {
@@ -433,6 +436,40 @@ __global__ void __launch_bounds__(256) tri_prepare_kernel(
     const bool keep = upper ? (cc >= r) : (cc <= r);
     dst[gi * kTriDiagBlock + cc] = (keep && gc < n) ? __ldg(src + gi * ld + gc) : 0.0f;
   }
+}
+
+// Table in the kernel's parameters (calls whose table must live in the
+// workspace, i.e. the allocation-free entry): the B blocks copy it there.
+__global__ void __launch_bounds__(256) tri_prepare_kernel(
+    const float* __restrict__ a, int64_t lda, const float* __restrict__ b, int64_t ldb, int64_t n,
+    int upper, float* __restrict__ adiag, float* __restrict__ bdiag, float* __restrict__ c,
+    int64_t ldc, const int2* __restrict__ split_tiles, int n_split, int block_m, int block_n,
+    int4* __restrict__ table_dst, const __grid_constant__ TableParam tp) {
+  // Launched with programmatic stream serialization: let the engine launch
+  // (it waits for this grid before reading), and wait for the previous
+  // kernel, which may still read the workspace this pass rewrites.
+  ptx::griddep_launch_dependents();
+  ptx::griddep_wait();
+  if (tp.words > 0) {
+    if (blockIdx.y == 1)   // B's blocks also copy the table (grid-stride over x)
+      for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tp.words; i += gridDim.x * blockDim.x)
+        table_dst[i] = tp.w[i];
+    split_tiles = reinterpret_cast<const int2*>(tp.w + tp.split_off);
+  }
+  tri_prepare_body(a, lda, b, ldb, n, upper, adiag, bdiag, c, ldc, split_tiles, nullptr, n_split,
+                   block_m, block_n);
+}
+
+// Table already resident (the per-device cache): small parameters only, so
+// the launch carries no 30 KB parameter block.
+__global__ void __launch_bounds__(256) tri_prepare_cached_kernel(
+    const float* __restrict__ a, int64_t lda, const float* __restrict__ b, int64_t ldb, int64_t n,
+    int upper, float* __restrict__ adiag, float* __restrict__ bdiag, float* __restrict__ c,
+    int64_t ldc, const int4* __restrict__ split4, int n_split, int block_m, int block_n) {
+  ptx::griddep_launch_dependents();
+  ptx::griddep_wait();
+  tri_prepare_body(a, lda, b, ldb, n, upper, adiag, bdiag, c, ldc, nullptr, split4, n_split,
+                   block_m, block_n);
 }
 
 // 3xTF32 pre-split of both operands in one launch (blockIdx.y: 0 = A,
@@ -1077,33 +1114,12 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     bdiag = reinterpret_cast<float*>(ws + nbytes);
     ws += 2 * nbytes;
     // Unit table (longest-first, split long tiles) followed by the split
-    // tiles' coordinates: one upload, then one pre-pass launch.
+    // tiles' coordinates.  Normal calls read it from the per-device cache
+    // (uploaded once per shape); allocation-free calls place it in their
+    // workspace through the pre-pass's parameters (or a copy when larger).
     const auto tri_ptr = cached_tri_table(d, pl.block_m, pl.block_n, pl.tiles_m, pl.tiles_n,
                                           pl.grid / pl.cluster_ctas, pl.tma_store);
     const TriTable& tri = *tri_ptr;
-    const int64_t tbytes = static_cast<int64_t>(tri.units.size()) * sizeof(int4);
-    const int64_t zbytes = static_cast<int64_t>(tri.split_tiles.size()) * sizeof(int2);
-    std::vector<char> host(round_up(tbytes, 256) + zbytes);
-    std::memcpy(host.data(), tri.units.data(), tbytes);
-    if (zbytes) std::memcpy(host.data() + round_up(tbytes, 256), tri.split_tiles.data(), zbytes);
-    table = reinterpret_cast<int4*>(ws);
-    const int2* split_list = reinterpret_cast<const int2*>(ws + round_up(tbytes, 256));
-    ws += round_up(tbytes, 256) + round_up(zbytes, 256);
-    // Small tables ride in the pre-pass's parameters (no copy engine, no
-    // staging of pageable memory); larger ones are copied.
-    static thread_local TableParam tparam;
-    const int64_t words = static_cast<int64_t>(host.size() + 15) / 16;
-    if (words <= kTableParamWords) {
-      host.resize(words * 16, 0);
-      tparam.words = static_cast<int>(words);
-      tparam.split_off = static_cast<int>(round_up(tbytes, 256) / 16);
-      std::memcpy(tparam.w, host.data(), host.size());
-    } else {
-      tparam.words = 0;
-      if (cudaMemcpyAsync(table, host.data(), host.size(), cudaMemcpyHostToDevice, stream) !=
-          cudaSuccess)
-        return B2G_ERR_LAUNCH;
-    }
     const int n_split = static_cast<int>(tri.split_tiles.size());
     const int64_t diag_blocks = cdiv(d->m, kTriDiagBlock) * (kTriDiagBlock / kTriDiagRows);
     const int64_t zero_blocks = static_cast<int64_t>(n_split) * cdiv(pl.block_m, kTriDiagRows);
@@ -1117,12 +1133,47 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = B2G_PDL ? 1 : 0;
-    if (cudaLaunchKernelEx(&cfg, tri_prepare_kernel, a, lda, b, ldb, static_cast<int64_t>(d->m),
-                           static_cast<int>(d->op == B2G_OP_TRI_UPPER), adiag, bdiag, d->c,
-                           static_cast<int64_t>(d->ldc), split_list, n_split,
-                           static_cast<int>(pl.block_m), static_cast<int>(pl.block_n), table,
-                           tparam) != cudaSuccess)
-      return B2G_ERR_LAUNCH;
+    const int upper = static_cast<int>(d->op == B2G_OP_TRI_UPPER);
+    if (!table_in_workspace) {
+      table = const_cast<int4*>(device_tri_table(tri_ptr));
+      if (!table) return B2G_ERR_LAUNCH;
+      const int4* split4 = table + tri.units.size();
+      if (cudaLaunchKernelEx(&cfg, tri_prepare_cached_kernel, a, lda, b, ldb,
+                             static_cast<int64_t>(d->m), upper, adiag, bdiag, d->c,
+                             static_cast<int64_t>(d->ldc), split4, n_split,
+                             static_cast<int>(pl.block_m),
+                             static_cast<int>(pl.block_n)) != cudaSuccess)
+        return B2G_ERR_LAUNCH;
+    } else {
+      const int64_t tbytes = static_cast<int64_t>(tri.units.size()) * sizeof(int4);
+      const int64_t zbytes = static_cast<int64_t>(tri.split_tiles.size()) * sizeof(int2);
+      std::vector<char> host(round_up(tbytes, 256) + zbytes);
+      std::memcpy(host.data(), tri.units.data(), tbytes);
+      if (zbytes) std::memcpy(host.data() + round_up(tbytes, 256), tri.split_tiles.data(), zbytes);
+      table = reinterpret_cast<int4*>(ws);
+      const int2* split_list = reinterpret_cast<const int2*>(ws + round_up(tbytes, 256));
+      ws += round_up(tbytes, 256) + round_up(zbytes, 256);
+      // Small tables ride in the pre-pass's parameters (no copy engine, no
+      // staging of pageable memory); larger ones are copied.
+      static thread_local TableParam tparam;
+      const int64_t words = static_cast<int64_t>(host.size() + 15) / 16;
+      if (words <= kTableParamWords) {
+        host.resize(words * 16, 0);
+        tparam.words = static_cast<int>(words);
+        tparam.split_off = static_cast<int>(round_up(tbytes, 256) / 16);
+        std::memcpy(tparam.w, host.data(), host.size());
+      } else {
+        tparam.words = 0;
+        if (cudaMemcpyAsync(table, host.data(), host.size(), cudaMemcpyHostToDevice, stream) !=
+            cudaSuccess)
+          return B2G_ERR_LAUNCH;
+      }
+      if (cudaLaunchKernelEx(&cfg, tri_prepare_kernel, a, lda, b, ldb, static_cast<int64_t>(d->m),
+                             upper, adiag, bdiag, d->c, static_cast<int64_t>(d->ldc), split_list,
+                             n_split, static_cast<int>(pl.block_m), static_cast<int>(pl.block_n),
+                             table, tparam) != cudaSuccess)
+        return B2G_ERR_LAUNCH;
+    }
   }
 
   // Triangular TF32 through the gated transform warps: the unit table from
@@ -1198,6 +1249,7 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   if (B2G_DYNAMIC_UNITS && d->op == B2G_OP_GEMM && d->k > 0 && pl.work_units > slots &&
       static_cast<int64_t>(pl.splits - 1) * pl.kb_per_split < p.kb_total) {
     p.sched = sched_slot();
+    p.early_draw = early_draw_on() ? 1 : 0;
   }
 
   // Split-K accumulates into C, which must start at zero: the first K piece

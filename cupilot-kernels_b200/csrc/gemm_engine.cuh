@@ -105,6 +105,10 @@ struct EngineParams {
   // operand, the rest go straight to the MMA.  0 = every stage is
   // transformed (3xTF32 split).
   int xf_gate;
+  // Dynamic schedule: the pair leader's producer draws unit i + 1 from the
+  // counter when it starts unit i, so the atomic's round trip overlaps
+  // unit i's loads instead of delaying the next unit's first stage.
+  int early_draw;
 };
 
 // Triangular masking of one operand box, for one CTA: 0 nothing masked,
@@ -680,10 +684,16 @@ __global__ void __launch_bounds__(
       const bool fetcher = units.dyn && leader;
       uint32_t it = 0;
       bool ok = true;
+      unsigned long long drawn = 0;
       for (uint32_t ui = 0; ok; ++ui) {
         long long w;
         if (fetcher) {
-          w = ui == 0 ? unit0 : unit_step + static_cast<long long>(atomicAdd(p.sched, 1ull));
+          if (ui == 0)
+            w = unit0;
+          else if (p.early_draw)
+            w = unit_step + static_cast<long long>(drawn);
+          else
+            w = unit_step + static_cast<long long>(atomicAdd(p.sched, 1ull));
           const int q = static_cast<int>(ui % kUnitQueue);
           *reinterpret_cast<volatile long long*>(&units.slots[q]) = w;
           ptx::mbar_arrive(&units.bars[q]);
@@ -692,6 +702,9 @@ __global__ void __launch_bounds__(
                                        static_cast<uint64_t>(w));
             ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_addr(&units.bars[q]), 1));
           }
+          // The next unit's index is only read at the top of the next
+          // iteration, so the warp does not wait for the atomic here.
+          if (p.early_draw && w < p.work_units) drawn = atomicAdd(p.sched, 1ull);
         } else if (!units.get(ui, w, abort_flag, p.wait_limit_ns)) {
           record_error(p.err, abort_flag, kErrWaitUnit);
           break;
