@@ -602,9 +602,10 @@ def _steps_for(ms_estimate, target_ms=300.0, lo=20, hi=400):
 
 def large_k_split(W, peaks, world, rank, warmup):
     """Large-K config with K split across the ranks (strong scaling: total K
-    fixed).  Each rank multiplies its K slice with the GEMM engine; the
-    256 x 256 partials are summed on rank 0 by the peer-memory reduction
-    (b2g_splitk_peer_reduce) at N > 1.  Inputs rotate over enough sets that
+    fixed).  At N > 1 each step is one kernel per rank
+    (b2g_gemm_splitk_peer): the rank's K-slice product, then, in the same
+    kernel, its 256 x 256 partial pushed to rank 0 over peer memory and
+    summed there.  Inputs rotate over enough sets that
     each call reads its operands from HBM.  At N > 1 rank 0 also times the
     whole config on its own GPU, for the efficiency t1 / (N t_N)."""
     part = _pkg("partition").Partitioner.from_env()
@@ -628,6 +629,11 @@ def large_k_split(W, peaks, world, rank, warmup):
     steps = 200
     total, _ = time_loop(step, steps, warmup, world, per_launch=False)
     ms_serial = total / steps
+    # The same steps as two kernels (GEMM, then the stand-alone peer-memory
+    # sum) on the same mailboxes, for comparison with the fused kernel.
+    step2 = rotating(lambda A, B: part.split_k_matmul(A, B, root=0, method="peer"), sets)
+    total2, _ = time_loop(step2, steps, warmup, world, per_launch=False)
+    ms_two = total2 / steps
     # Pipelined: each step's cross-GPU sum runs on a side stream and overlaps
     # the next step's GEMM; the timed region ends after the last sum (join).
     astep = rotating(lambda A, B: part.split_k_matmul_async(A, B, root=0), sets)
@@ -655,9 +661,10 @@ def large_k_split(W, peaks, world, rank, warmup):
     out = {"ms": round(ms, 4), "tflops": round(w.flops / (ms / 1e3) / 1e12, 2),
            "gbs": round(w.min_bytes / (ms / 1e3) / 1e9, 1), "k_per_rank": k1 - k0,
            "input_sets": nsets,
-           "reduce": "peer-memory push to rank 0, one step at a time" if world > 1
-                     else "none (one GPU)"}
+           "reduce": "fused into the GEMM kernel: peer-memory push to rank 0, one step at a time"
+                     if world > 1 else "none (one GPU)"}
     if world > 1:
+        out["ms_two_kernels"] = round(ms_two, 4)  # GEMM + stand-alone peer sum (information)
         out["ms_pipelined"] = round(ms_pipe, 4)   # sums on a side stream (information)
     if rank == 0:
         out["parity"] = _sig(_rel(C, A_full.double() @ B_full.double()))

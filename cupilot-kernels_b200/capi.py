@@ -106,6 +106,9 @@ def lib(path: Path | None = None) -> C.CDLL:
                                              C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_int,
                                              C.c_int64, C.c_void_p]
         h.b2g_splitk_peer_reduce.restype = C.c_int
+        h.b2g_gemm_splitk_peer.argtypes = [C.POINTER(GemmDesc), C.POINTER(C.c_void_p), C.c_int,
+                                           C.c_int, C.c_int, C.c_int64, C.c_void_p]
+        h.b2g_gemm_splitk_peer.restype = C.c_int
         h.b2g_read_device_error.argtypes = [C.c_int, C.POINTER(C.c_int32)]
         h.b2g_read_device_error.restype = C.c_int
         h.b2g_status_string.argtypes = [C.c_int]
@@ -214,12 +217,27 @@ def splitk_peer_reduce(partial: int, out: int, elems: int, mailboxes, rank: int,
                                         epoch, C.c_void_p(stream))
 
 
+def gemm_splitk_peer(desc: GemmDesc, mailboxes, rank: int, root: int, epoch: int,
+                     stream: int = 0) -> int:
+    arr = (C.c_void_p * len(mailboxes))(*mailboxes)
+    return lib().b2g_gemm_splitk_peer(C.byref(desc), arr, len(mailboxes), rank, root, epoch,
+                                      C.c_void_p(stream))
+
+
 def torch_splitk_peer_reduce(t, mailboxes, rank, root, epoch):
     """b2g_splitk_peer_reduce through the Torch extension (no ctypes
     conversion per call): t is the root's output or another rank's partial."""
     from . import native
 
     native().splitk_peer_reduce(t, list(mailboxes), rank, root, epoch)
+
+
+def torch_gemm_splitk_peer(A, B, mailboxes, rank, root, epoch):
+    """b2g_gemm_splitk_peer through the Torch extension: A, B this rank's
+    K slices; returns C (the sum on the root, the partial elsewhere)."""
+    from . import native
+
+    return native().splitk_peer_matmul(A, B, list(mailboxes), rank, root, epoch)
 
 
 def read_device_error(device: int = 0) -> int:

@@ -1035,7 +1035,8 @@ int64_t tri_gate_table_bytes(const b2g_gemm_desc* d, const b2g_gemm_plan& pl) {
 // per-device cache.
 static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* workspace,
                        int* err_word, cudaStream_t stream, const float* row_bias = nullptr,
-                       bool table_in_workspace = false) {
+                       bool table_in_workspace = false,
+                       const EngineParams::Xgpu* xgpu = nullptr) {
   const float* a = d->a;
   const float* b = d->b;
   int64_t lda = d->lda, ldb = d->ldb, sa = d->stride_a, sb = d->stride_b;
@@ -1242,6 +1243,7 @@ static int run_planned(const b2g_gemm_desc* d, const b2g_gemm_plan& pl, void* wo
   p.diag_oob_row = static_cast<int>(d->m);
   p.row_bias = row_bias;
   p.err = err_word;
+  if (xgpu) p.xg = *xgpu;
   p.trace = trace_pointer();
   // Dynamic schedule: plain GEMMs with more units than CTAs (pairs), every
   // unit holding at least one K block (no structurally empty units).
@@ -1369,6 +1371,48 @@ extern "C" int b2g_gemm(const b2g_gemm_desc* d, b2g_stream_t stream_handle) {
   if (pl.workspace_bytes > 0 && (!d->workspace || d->workspace_bytes < pl.workspace_bytes))
     return B2G_ERR_WORKSPACE;
   return run_planned(d, pl, d->workspace, ds->err_word, stream);
+}
+
+extern "C" int b2g_gemm_splitk_peer(const b2g_gemm_desc* d, void* const* mailboxes, int world,
+                                    int rank, int root, int64_t epoch,
+                                    b2g_stream_t stream_handle) {
+  if (!valid_desc(d)) return B2G_ERR_INVALID_ARG;
+  if (world < 1 || world > kPeerMaxRanks || rank < 0 || rank >= world || root < 0 ||
+      root >= world || epoch < 1 || !mailboxes)
+    return B2G_ERR_INVALID_ARG;
+  if (world == 1) return b2g_gemm(d, stream_handle);
+  // One contiguous M x N output (the protocol moves it as a flat array).
+  if (d->op != B2G_OP_GEMM || d->batch != 1 || d->ldc != d->n || d->m == 0 || d->n == 0)
+    return B2G_ERR_UNSUPPORTED;
+  if (reinterpret_cast<uintptr_t>(d->c) % 16) return B2G_ERR_UNSUPPORTED;
+  for (int r = 0; r < world; ++r)
+    if (!mailboxes[r]) return B2G_ERR_INVALID_ARG;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  DeviceState* ds = nullptr;
+  int rc = device_state(&ds);
+  if (rc != B2G_OK) return rc;
+  b2g_gemm_plan pl;
+  rc = b2g_gemm_plan_for(d, ds->num_sms, &pl);
+  if (rc != B2G_OK) return rc;
+  if (pl.workspace_bytes > 0 && (!d->workspace || d->workspace_bytes < pl.workspace_bytes))
+    return B2G_ERR_WORKSPACE;
+  const int64_t elems = d->m * d->n;
+  const PeerLayout lay = peer_layout(elems, world);
+  EngineParams::Xgpu x;
+  std::memset(&x, 0, sizeof(x));
+  for (int r = 0; r < world; ++r) x.mbox[r] = static_cast<unsigned char*>(mailboxes[r]);
+  x.epoch = epoch;
+  x.elems = elems;
+  x.nchunk = lay.nchunk;
+  x.ready_off = lay.ready_off;
+  x.consumed_off = lay.consumed_off;
+  x.count_off = lay.count_off;
+  x.landing_off = lay.landing_off;
+  x.slot_stride = lay.slot_stride;
+  x.world = world;
+  x.rank = rank;
+  x.root = root;
+  return run_planned(d, pl, d->workspace, ds->err_word, stream, nullptr, false, &x);
 }
 
 namespace b2g {

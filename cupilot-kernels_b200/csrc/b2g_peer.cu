@@ -21,8 +21,8 @@
 // Every wait is bounded (B2G_WAIT_LIMIT_MS): a wait that gives up records a
 // code in the device error word and the CTA returns; nothing traps.  Only
 // plain loads and stores touch peer memory (no TMA, no bulk copies, no
-// multicast), and only the mailboxes do: the GEMM engine never sees a peer
-// pointer.
+// multicast), and only the mailboxes do.  b2g_gemm_splitk_peer runs the same
+// protocol inside the GEMM engine's epilogue (gemm_engine.cuh, xgpu_exchange).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -31,56 +31,29 @@
 
 #include "../../include/b2g_gemm.h"
 #include "b2g_internal.h"
+#include "peer_protocol.cuh"
 #include "ptx_sm100.cuh"
 
 namespace {
 
+using b2g::kErrPeerCredit;
+using b2g::kErrPeerReady;
+using b2g::peer_layout;
+using Layout = b2g::PeerLayout;
 constexpr int kThreads = 256;
 constexpr int64_t kChunk = kThreads * 4;   // floats per chunk: one float4 per thread
+static_assert(kChunk == b2g::kPeerChunk, "push / reduce kernels move one protocol chunk per CTA");
 constexpr int kMaxRanks = B2G_PEER_MAX_RANKS;
+static_assert(kMaxRanks == b2g::kPeerMaxRanks, "rank limit");
 
-enum : int { kErrPeerCredit = 0x201, kErrPeerReady = 0x202 };
+Layout layout(int64_t elems, int world) { return peer_layout(elems, world); }
 
-inline int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
-inline int64_t round_up(int64_t a, int64_t b) { return cdiv(a, b) * b; }
-
-// Mailbox layout for `elems` floats and `world` ranks:
-//   [0, flag_bytes)   ready[nchunk][world] u64, then consumed[nchunk] u64
-//   [flag_bytes, ..)  landing[2][world][elems] floats (read on the root only)
-struct Layout {
-  int64_t nchunk, ready_off, consumed_off, flag_bytes, landing_off, slot_stride, total;
-};
-Layout layout(int64_t elems, int world) {
-  Layout l;
-  l.nchunk = cdiv(elems, kChunk);
-  l.ready_off = 0;
-  l.consumed_off = l.nchunk * world * 8;
-  l.flag_bytes = round_up(l.consumed_off + l.nchunk * 8, 256);
-  l.landing_off = l.flag_bytes;
-  l.slot_stride = round_up(elems * 4, 256);             // bytes per (slot, rank) region
-  l.total = l.landing_off + 2 * world * l.slot_stride;
-  return l;
-}
-
-__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+  b2g::peer_st_release_sys(p, v);
 }
-
-// Spin (with a short sleep) until *flag >= want; false after limit_ns.
 __device__ __forceinline__ bool wait_at_least(const uint64_t* flag, uint64_t want,
                                               long long limit_ns) {
-  if (ld_acquire_sys(flag) >= want) return true;
-  const uint64_t t0 = b2g::ptx::globaltimer_ns();
-  for (unsigned spin = 0; ld_acquire_sys(flag) < want; ++spin) {
-    if (b2g::ptx::globaltimer_ns() - t0 > static_cast<uint64_t>(limit_ns)) return false;
-    if (spin > 64) __nanosleep(32);   // poll tight first: the flag usually lands within ~1 us
-  }
-  return true;
+  return b2g::peer_wait_at_least(flag, want, limit_ns);
 }
 
 struct PeerArgs {

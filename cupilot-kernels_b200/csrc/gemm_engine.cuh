@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "peer_protocol.cuh"
 #include "ptx_sm100.cuh"
 
 namespace b2g {
@@ -109,6 +110,23 @@ struct EngineParams {
   // counter when it starts unit i, so the atomic's round trip overlaps
   // unit i's loads instead of delaying the next unit's first stage.
   int early_draw;
+  // Fused cross-GPU K-split (xg.world > 1): this launch multiplies one
+  // rank's K slice into C (its partial, M x N contiguous) and then sums the
+  // ranks' partials on the root inside the same kernel, over the mailboxes
+  // of peer_protocol.cuh: once every CTA's stores are complete (a grid-wide
+  // count in this rank's mailbox), the epilogue warps of CTA i take protocol
+  // chunks i, i + grid, ...: a non-root rank copies them into its landing
+  // slot in the root's mailbox and stamps ready; the root waits for every
+  // rank's ready, adds the landed chunks to its own in rank order and stamps
+  // consumed.  Same flags, slots and order of additions as the stand-alone
+  // push / reduce kernels, so the two paths give identical sums.  Only plain
+  // loads and stores touch peer memory.
+  struct Xgpu {
+    unsigned char* mbox[kPeerMaxRanks];   // every rank's mailbox as mapped here
+    long long epoch, elems;
+    long long nchunk, ready_off, consumed_off, count_off, landing_off, slot_stride;
+    int world, rank, root;
+  } xg;
 };
 
 // Triangular masking of one operand box, for one CTA: 0 nothing masked,
@@ -574,6 +592,147 @@ __device__ __forceinline__ void store_group_tma(const EngineParams& p, const CUt
       }
     }
     ptx::bulk_commit();
+  }
+}
+
+// Barrier among the epilogue warps only (named barrier 1; the other roles
+// never take part).
+__device__ __forceinline__ void epi_bar_sync(int threads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The fused cross-GPU exchange (EngineParams::Xgpu), run by the `threads`
+// epilogue threads of every CTA after their last store; t = thread index
+// among them, flag = a shared-memory word for broadcasting.
+__device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, int t,
+                                           volatile int* abort_flag, volatile int* flag) {
+  const EngineParams::Xgpu& x = p.xg;
+  // 1. This thread's bulk stores (TMA stores / reduce-adds) are complete in
+  //    global memory and visible to generic-proxy loads of any SM.
+  if ((t & 31) == 0) ptx::bulk_wait_all();
+  __syncwarp();
+  ptx::fence_proxy_async_global();
+  __threadfence();
+  epi_bar_sync(threads);
+  // 2. Grid-wide arrival in this rank's mailbox.  The count word carries the
+  //    epoch in its upper bits: a word left by another epoch (or by a launch
+  //    that gave up) counts as zero.
+  unsigned long long* cnt = reinterpret_cast<unsigned long long*>(x.mbox[x.rank] + x.count_off);
+  const unsigned long long tag = static_cast<unsigned long long>(x.epoch) << 20;
+  if (t == 0) {
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(cnt), seen;
+    do {
+      seen = old;
+      const unsigned long long nv = (seen >> 20) == (tag >> 20) ? seen + 1 : tag + 1;
+      old = atomicCAS(cnt, seen, nv);
+    } while (old != seen);
+    const unsigned long long want = tag + gridDim.x;
+    const uint64_t t0 = ptx::globaltimer_ns();
+    int ok = 1;
+    while (ld_acquire_gpu_u64(cnt) != want) {
+      if (*abort_flag || ptx::globaltimer_ns() - t0 > static_cast<uint64_t>(p.wait_limit_ns)) {
+        ok = 0;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (!ok && !*abort_flag) record_error(p.err, abort_flag, kErrPeerGrid);
+    *flag = ok && !*abort_flag;
+  }
+  epi_bar_sync(threads);
+  if (!*flag) return;
+  __threadfence();
+  const bool is_root = x.rank == x.root;
+  const long long slot = x.epoch & 1;
+  const float* own = p.C;
+  unsigned char* rootb = x.mbox[x.root];
+  for (long long c = blockIdx.x; c < x.nchunk; c += gridDim.x) {
+    const long long i0 = c * kPeerChunk;
+    const long long i1 = i0 + kPeerChunk < x.elems ? i0 + kPeerChunk : x.elems;
+    if (!is_root) {
+      // The slot this epoch writes was last read by the root two epochs ago.
+      if (t == 0) {
+        const uint64_t* consumed =
+            reinterpret_cast<const uint64_t*>(x.mbox[x.rank] + x.consumed_off) + c;
+        const long long need = x.epoch - 2;
+        const int ok = need <= 0 || peer_wait_at_least(consumed, static_cast<uint64_t>(need),
+                                                       p.wait_limit_ns);
+        if (!ok) record_error(p.err, abort_flag, kErrPeerCredit);
+        *flag = ok;
+      }
+      epi_bar_sync(threads);
+      if (!*flag) return;
+      float* dst = reinterpret_cast<float*>(rootb + x.landing_off +
+                                            (slot * x.world + x.rank) * x.slot_stride);
+      for (long long i = i0 + 4ll * t; i < i1; i += 4ll * threads) {
+        if (i + 4 <= i1) {
+          *reinterpret_cast<float4*>(dst + i) = __ldcg(reinterpret_cast<const float4*>(own + i));
+        } else {
+          for (long long j = i; j < i1; ++j) dst[j] = __ldcg(own + j);
+        }
+      }
+      // The barrier orders every thread's peer stores before thread 0's
+      // release store (cumulative at system scope).
+      epi_bar_sync(threads);
+      if (t == 0) {
+        uint64_t* ready = reinterpret_cast<uint64_t*>(rootb + x.ready_off) + c * x.world + x.rank;
+        peer_st_release_sys(ready, static_cast<uint64_t>(x.epoch));
+      }
+    } else {
+      if (t == 0) *flag = 1;
+      epi_bar_sync(threads);
+      if (t < x.world && t != x.root) {
+        const uint64_t* ready = reinterpret_cast<const uint64_t*>(rootb + x.ready_off) +
+                                c * x.world + t;
+        if (!peer_wait_at_least(ready, static_cast<uint64_t>(x.epoch), p.wait_limit_ns)) {
+          *flag = 0;
+          record_error(p.err, abort_flag, kErrPeerReady);
+        }
+      }
+      epi_bar_sync(threads);
+      if (!*flag) return;
+      const float* land = reinterpret_cast<const float*>(rootb + x.landing_off +
+                                                         slot * x.world * x.slot_stride);
+      const long long stride = x.slot_stride / 4;
+      float* out = p.C;
+      for (long long i = i0 + 4ll * t; i < i1; i += 4ll * threads) {
+        if (i + 4 <= i1) {
+          float4 acc = __ldcg(reinterpret_cast<const float4*>(out + i));
+          float4 v[kPeerMaxRanks];
+#pragma unroll
+          for (int r = 0; r < kPeerMaxRanks; ++r)
+            if (r < x.world && r != x.root)
+              v[r] = __ldcg(reinterpret_cast<const float4*>(land + r * stride + i));
+#pragma unroll
+          for (int r = 0; r < kPeerMaxRanks; ++r)
+            if (r < x.world && r != x.root) {
+              acc.x += v[r].x;
+              acc.y += v[r].y;
+              acc.z += v[r].z;
+              acc.w += v[r].w;
+            }
+          *reinterpret_cast<float4*>(out + i) = acc;
+        } else {
+          for (long long j = i; j < i1; ++j) {
+            float acc = __ldcg(out + j);
+            for (int r = 0; r < x.world; ++r)
+              if (r != x.root) acc += __ldcg(land + r * stride + j);
+            out[j] = acc;
+          }
+        }
+      }
+      epi_bar_sync(threads);   // every thread's reads of the slot are done
+      if (t < x.world && t != x.root) {
+        uint64_t* consumed = reinterpret_cast<uint64_t*>(x.mbox[t] + x.consumed_off) + c;
+        peer_st_release_sys(consumed, static_cast<uint64_t>(x.epoch));
+      }
+    }
   }
 }
 
@@ -1211,7 +1370,13 @@ __global__ void __launch_bounds__(
       if (trace && ew == 0 && lane == 0) trace[5] = ptx::globaltimer_ns();
       ++tl;
     }
-    if (lane == 0) ptx::bulk_wait_read<0>();   // staging boxes read before the CTA exits
+    if (p.xg.world > 1) {
+      // Fused cross-GPU step (every CTA takes part, also one without units).
+      xgpu_exchange(p, Cfg::kEpiWarps * 32, ew * 32 + lane, abort_flag,
+                    reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 8));
+    } else if (lane == 0) {
+      ptx::bulk_wait_read<0>();   // staging boxes read before the CTA exits
+    }
   } else if (XF) {
     // ------------------------------------------------------------ transform
     // Each CTA transforms its own slices (A rows m_cta.., B columns n_cta..)

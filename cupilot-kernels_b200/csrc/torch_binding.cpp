@@ -421,6 +421,56 @@ void splitk_peer_reduce(at::Tensor t, std::vector<int64_t> mailboxes, int64_t ra
                "b2g_splitk_peer_reduce");
 }
 
+// This rank's K-slice product and the cross-GPU sum in one kernel
+// (b2g_gemm_splitk_peer): A (M x K_r), B (K_r x N) this rank's slices, both
+// row-major or transposed views; returns C (M x N), which on the root holds
+// the full sum after the call and elsewhere this rank's partial.
+at::Tensor splitk_peer_matmul(at::Tensor A, at::Tensor B, std::vector<int64_t> mailboxes,
+                              int64_t rank, int64_t root, int64_t epoch) {
+  check_input(A, "A");
+  check_input(B, "B");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2, "A and B must be 2-D");
+  TORCH_CHECK(A.device() == B.device(), "A and B must be on the same device");
+  TORCH_CHECK(A.size(1) == B.size(0), "inner dimensions differ: A is ", A.sizes(), ", B is ",
+              B.sizes());
+  const c10::cuda::CUDAGuard guard(A.device());
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(1);
+  at::Tensor C = at::empty({M, N}, A.options());
+  if (M == 0 || N == 0) return C;
+  Operand a = as_operand(A), b = as_operand(B);
+  b2g_gemm_desc d{};
+  d.op = B2G_OP_GEMM;
+  d.precision = precision_now();
+  d.m = M;
+  d.n = N;
+  d.k = K;
+  d.batch = 1;
+  d.a = a.ptr;
+  d.lda = a.ld;
+  d.trans_a = a.trans;
+  d.b = b.ptr;
+  d.ldb = b.ld;
+  d.trans_b = b.trans;
+  d.c = C.data_ptr<float>();
+  d.ldc = N;
+  const int64_t ws = b2g_gemm_workspace_bytes(&d);
+  TORCH_CHECK(ws >= 0, "b2g: invalid GEMM descriptor");
+  at::Tensor wst;
+  if (ws > 0) {
+    wst = at::empty({ws}, A.options().dtype(at::kByte));
+    d.workspace = wst.data_ptr();
+    d.workspace_bytes = ws;
+  }
+  std::vector<void*> boxes(mailboxes.size());
+  for (size_t r = 0; r < mailboxes.size(); ++r) boxes[r] = reinterpret_cast<void*>(mailboxes[r]);
+  auto stream = at::cuda::getCurrentCUDAStream(A.device().index());
+  check_status(b2g_gemm_splitk_peer(&d, boxes.data(), static_cast<int>(boxes.size()),
+                                    static_cast<int>(rank), static_cast<int>(root), epoch,
+                                    stream.stream()),
+               "b2g_gemm_splitk_peer");
+  return C;
+}
+
 int64_t read_device_error(int64_t device) {
   int32_t code = 0;
   check_status(b2g_read_device_error(static_cast<int>(device), &code), "b2g_read_device_error");
@@ -462,4 +512,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("get_thread_precision", &get_thread_precision);
   m.def("read_device_error", &read_device_error);
   m.def("splitk_peer_reduce", &splitk_peer_reduce, "one epoch of the cross-GPU K-split sum");
+  m.def("splitk_peer_matmul", &splitk_peer_matmul,
+        "this rank's K-slice product and the cross-GPU sum, one kernel");
 }

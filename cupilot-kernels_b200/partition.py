@@ -120,10 +120,20 @@ class Partitioner:
         """Given this rank's K slice (A[:, K_r], B[K_r, :]), return C = A B on
         the root (None elsewhere), or on every rank when all_ranks.
 
-        method: "peer" sums the partials with the peer-memory reduction (CUDA
-        tensors, one node), "collective" with one NCCL / gloo reduce; "auto"
-        picks "peer" for CUDA tensors on more than one rank unless all_ranks.
+        method: "fused" runs this rank's product and the peer-memory sum in one
+        kernel (b2g_gemm_splitk_peer; CUDA tensors, one node), "peer" runs the
+        product and then the stand-alone peer-memory reduction, "collective"
+        one NCCL / gloo reduce; "auto" picks "fused" for CUDA tensors on more
+        than one rank unless all_ranks.
         """
+        if method == "auto" and A_k.is_cuda and self.world > 1 and not all_ranks:
+            method = "fused"
+        if method == "fused":
+            if all_ranks:
+                raise ValueError("the peer reduction delivers C to the root only")
+            red = self.peer_reducer(A_k.shape[0] * B_k.shape[1])
+            C = red.matmul(A_k, B_k, root)
+            return C if self.rank == root else None
         if A_k.shape[1] == 0:
             part = torch.zeros(A_k.shape[0], B_k.shape[1], dtype=A_k.dtype, device=A_k.device)
         else:
@@ -230,6 +240,18 @@ class PeerReducer:
                                              stream)
         if rc != 0:
             raise RuntimeError(f"b2g_splitk_peer_reduce failed (status {rc})")
+
+    def matmul(self, A_k: torch.Tensor, B_k: torch.Tensor, root: int = 0) -> torch.Tensor:
+        """One epoch as a single kernel: this rank's slice product A_k B_k and
+        the cross-GPU sum (b2g_gemm_splitk_peer).  Returns the product tensor:
+        the full sum on the root, this rank's partial elsewhere."""
+        if A_k.shape[0] * B_k.shape[1] != self.elems:
+            raise ValueError("the product's size differs from the mailbox's")
+        self.epoch += 1
+        fused = getattr(self.backend, "torch_gemm_splitk_peer", None)
+        if fused is None:
+            raise RuntimeError("the fused K-split needs the Torch extension's binding")
+        return fused(A_k, B_k, self.mailboxes, self.part.rank, root, self.epoch)
 
     def close(self) -> None:
         for r, ptr in enumerate(self.mailboxes):

@@ -32,7 +32,8 @@
  *   kernels/5_Matrix_scalar_multiplication_best_kernel.cu:47    matrix_scalar_mult_cuda  -> b2g_scale
  *   kernels/87_conv_pointwise_2D_best_kernel.cu:451             pointwise_conv_cuda      -> b2g_pointwise_conv
  *   kernels/97_ScaledDotProductAttention_best_kernel.cu:256     fused_attention_cuda     -> b2g_sdpa
- *   kernels/6_Matmul_with_large_K_dimension_best_kernel.cu:147-200 (streams + C.add_) -> b2g_splitk_peer_reduce
+ *   kernels/6_Matmul_with_large_K_dimension_best_kernel.cu:147-200 (streams + C.add_) -> b2g_splitk_peer_reduce,
+ *                                                                  or with the product: b2g_gemm_splitk_peer
  *
  * Error behaviour: every entry point returns a b2g_status; 0 is success.
  * Nothing traps or asserts on the device.  Kernel-side waits are bounded;
@@ -267,6 +268,26 @@ B2G_API int b2g_peer_mailbox_destroy(void* mailbox);   /* a mailbox this process
 B2G_API int b2g_splitk_peer_reduce(const float* partial, float* out, int64_t elems,
                                    void* const* mailboxes, int world, int rank, int root,
                                    int64_t epoch, b2g_stream_t stream);
+
+/*
+ * The K-split product and its cross-GPU sum in ONE kernel: this rank's
+ * slice C_r = A[:, K_r] B[K_r, :] (d: a plain GEMM, batch 1, C contiguous
+ * M x N with ldc == n, 16-byte aligned) is computed into d->c, and once every
+ * CTA's stores are complete the same kernel's epilogue warps move it over
+ * NVLink: a non-root rank copies it chunk by chunk into its landing slot in
+ * the root's mailbox; the root adds the landed chunks, in rank order, to its
+ * own C.  The mailboxes, epochs and flags are those of
+ * b2g_splitk_peer_reduce (mailboxes of b2g_peer_mailbox_bytes(m * n, world)),
+ * and the sum is bit-identical to b2g_gemm followed by
+ * b2g_splitk_peer_reduce; the two paths may alternate epoch by epoch.
+ * Replaces the same reference step as b2g_splitk_peer_reduce
+ * (kernels/6_Matmul_with_large_K_dimension_best_kernel.cu:147-200) together
+ * with the product before it (:128).  A bounded wait that gives up records
+ * 0x201 / 0x202, or 0x203 for the grid-wide arrival, in the device error
+ * word.  world == 1 is b2g_gemm.
+ */
+B2G_API int b2g_gemm_splitk_peer(const b2g_gemm_desc* d, void* const* mailboxes, int world,
+                                 int rank, int root, int64_t epoch, b2g_stream_t stream);
 
 /* Read and clear the device-side error word of `device` (synchronises it). */
 B2G_API int b2g_read_device_error(int device, int32_t* code);

@@ -14,9 +14,14 @@
   GEMM in the same context is correct.
 * Two GPUs (skipped with fewer): torchrun with two ranks runs the large-K
   product split over K through Partitioner.split_k_matmul(method="peer"),
-  three calls in a row, then three pipelined calls (split_k_matmul_async:
+  three calls in a row, three through the fused kernel (method="fused",
+  b2g_gemm_splitk_peer), then three pipelined calls (split_k_matmul_async:
   the sums on a side stream behind the GEMMs) and a join, each result
   checked on the root against a float64 product.
+* One GPU, fused kernel: b2g_gemm_splitk_peer with two emulated ranks run
+  one after the other (rank 1 first), epochs alternating with the
+  stand-alone path on the same mailboxes; and its bounded wait as the root
+  of an epoch nobody pushed.
 """
 import json
 import os
@@ -63,6 +68,55 @@ def test_peer_reduce_protocol_on_one_gpu(capi, ops):
             capi.peer_mailbox_destroy(p)
 
 
+@pytest.mark.parametrize("k", [256, 65536])
+def test_fused_splitk_peer_on_one_gpu(capi, ops, k):
+    """b2g_gemm_splitk_peer (product and cross-GPU sum in one kernel) with
+    two emulated ranks on one device, rank 1 first, the device synchronised
+    between the calls; epochs alternate between the fused path and the
+    stand-alone GEMM + b2g_splitk_peer_reduce on the same mailboxes.  At
+    k = 256 no launch splits K, so every partial is deterministic and the
+    root's sum must equal P0 + P1 bit for bit; at k = 65536 (split-K inside
+    each rank) the sum is checked against the fp64 oracle."""
+    m = n = 256
+    elems = m * n
+    mb = [capi.peer_mailbox_create(elems, 2)[0] for _ in range(2)]
+    stream = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(5)
+    native = import_pkg().native()
+    try:
+        for epoch in range(1, 7):
+            A = torch.randn(m, k, generator=g, device="cuda")
+            B = torch.randn(k, n, generator=g, device="cuda")
+            h = k // 2
+            A1, B1 = A[:, h:].contiguous(), B[h:].contiguous()
+            A0, B0 = A[:, :h].contiguous(), B[:h].contiguous()
+            fused = epoch % 2 == 1
+            if fused:
+                C1 = native.splitk_peer_matmul(A1, B1, mb, 1, 0, epoch)
+                torch.cuda.synchronize()      # rank 1's kernel has finished
+                P1 = C1.clone()
+                out = native.splitk_peer_matmul(A0, B0, mb, 0, 0, epoch)
+                torch.cuda.synchronize()
+            else:
+                P1 = ops.p2.forward(A1, B1)
+                rc = capi.splitk_peer_reduce(P1.data_ptr(), 0, elems, mb, 1, 0, epoch, stream)
+                assert rc == capi.B2G_OK, capi.status_string(rc)
+                torch.cuda.synchronize()
+                out = ops.p2.forward(A0, B0)
+                rc = capi.splitk_peer_reduce(0, out.data_ptr(), elems, mb, 0, 0, epoch, stream)
+                assert rc == capi.B2G_OK, capi.status_string(rc)
+                torch.cuda.synchronize()
+            if k == 256:
+                P0 = ops.p2.forward(A0, B0)
+                assert torch.equal(out, P0 + P1), epoch
+            err = O.rel_fro(out.double().cpu().numpy(), O.large_k(A.cpu().numpy(), B.cpu().numpy()))
+            assert err <= O.TOL["tf32"], (epoch, err)
+        assert ops.read_device_error(torch.cuda.current_device()) == 0
+    finally:
+        for p in mb:
+            capi.peer_mailbox_destroy(p)
+
+
 TIMEOUT_CHILD = r"""
 import importlib, json, sys, time, torch
 sys.path.insert(0, sys.argv[1])
@@ -87,6 +141,47 @@ print(json.dumps({"rc": rc, "code": code, "waited": waited, "err_after": err,
                   "out_untouched": bool((out == 0).all().item()),
                   "code_after": ops.read_device_error(0)}))
 """
+
+
+FUSED_TIMEOUT_CHILD = r"""
+import importlib, json, sys, time, torch
+sys.path.insert(0, sys.argv[1])
+ops = importlib.import_module("cupilot-kernels_b200.ops")
+capi = importlib.import_module("cupilot-kernels_b200.capi")
+native = importlib.import_module("cupilot-kernels_b200").native()
+m = n = 128
+mb = [capi.peer_mailbox_create(m * n, 2)[0] for _ in range(2)]
+A = torch.randn(m, 512, device="cuda"); B = torch.randn(512, n, device="cuda")
+t0 = time.time()
+C = native.splitk_peer_matmul(A, B, mb, 0, 0, 1)     # root of an epoch nobody pushed
+torch.cuda.synchronize()
+waited = time.time() - t0
+code = ops.read_device_error(0)
+ref = A.double() @ B.double()
+own = float(((C.double() - ref).norm() / ref.norm()).item())   # only its own partial
+A2 = torch.randn(300, 200, device="cuda"); B2 = torch.randn(200, 100, device="cuda")
+C2 = ops.p2.forward(A2, B2)
+ref2 = A2.double() @ B2.double()
+err = float(((C2.double() - ref2).norm() / ref2.norm()).item())
+for p in mb:
+    capi.peer_mailbox_destroy(p)
+print(json.dumps({"code": code, "waited": waited, "own": own, "err_after": err,
+                  "code_after": ops.read_device_error(0)}))
+"""
+
+
+def test_fused_splitk_bounded_wait_reports_and_context_survives():
+    """The fused kernel as root of an epoch no rank pushed: its wait for the
+    ready flags gives up after B2G_WAIT_LIMIT_MS, records 0x202 and the
+    kernel ends with the root's own partial in C; the next GEMM is correct."""
+    env = dict(os.environ, B2G_WAIT_LIMIT_MS="50")
+    r = subprocess.run([sys.executable, "-c", FUSED_TIMEOUT_CHILD, str(REPO)], env=env,
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = json.loads(r.stdout.strip().splitlines()[-1])
+    assert out["code"] == 0x202 and out["waited"] < 30, out
+    assert out["own"] <= 1e-2, out
+    assert out["err_after"] <= 1e-2 and out["code_after"] == 0, out
 
 
 def test_peer_reduce_bounded_wait_reports_and_context_survives():
@@ -116,6 +211,19 @@ for step in range(3):
     B = torch.randn(k, n, generator=g, device="cuda")
     k0, k1 = p.k_range(k)
     C = p.split_k_matmul(A[:, k0:k1].contiguous(), B[k0:k1].contiguous(), root=0, method="peer")
+    torch.cuda.synchronize()
+    if p.rank == 0:
+        ref = A.double() @ B.double()
+        res.append(float(((C.double() - ref).norm() / ref.norm()).item()))
+    else:
+        assert C is None
+# Fused: product and cross-GPU sum in one kernel per step.
+for step in range(3):
+    g = torch.Generator(device="cuda").manual_seed(300 + step)
+    A = torch.randn(m, k, generator=g, device="cuda")
+    B = torch.randn(k, n, generator=g, device="cuda")
+    k0, k1 = p.k_range(k)
+    C = p.split_k_matmul(A[:, k0:k1].contiguous(), B[k0:k1].contiguous(), root=0, method="fused")
     torch.cuda.synchronize()
     if p.rank == 0:
         ref = A.double() @ B.double()
@@ -159,4 +267,4 @@ def test_peer_reduce_two_gpus(tmp_path):
     assert r.returncode == 0, r.stderr[-3000:]
     out = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
     assert out["codes"] == [0, 0], out
-    assert len(out["errs"]) == 6 and max(out["errs"]) <= 1e-2, out
+    assert len(out["errs"]) == 9 and max(out["errs"]) <= 1e-2, out
