@@ -91,7 +91,8 @@ struct EngineParams {
   // last unit: TMEM data in registers, store issued (pairs of stamps);
   // MMA warp totals 16 ns spent waiting for operand stages, 17 ns waiting
   // for a free accumulator buffer, 18 units; 20 + 2u / 21 + 2u: unit u's
-  // first operand stage landed / last MMA issued (u < 20).
+  // first operand stage landed / last MMA issued (u < 20); 60-62 the fused
+  // cross-GPU step: stores complete, grid arrival seen, exchange done.
   unsigned long long* trace;
   // Triangular unit tables with split tiles: their (tm, tn) in .x / .y of
   // n_split entries.  Every CTA (pair) first zeroes its share of them (tile
@@ -610,8 +611,12 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
 // The fused cross-GPU exchange (EngineParams::Xgpu), run by the `threads`
 // epilogue threads of every CTA after their last store; t = thread index
 // among them, flag = a shared-memory word for broadcasting.
+// credit_ok: the non-root's slot credits, checked at the epilogue's start.
+// trace (tuning aid): words 60 stores complete, 61 grid arrival seen,
+// 62 exchange done (thread 0).
 __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, int t,
-                                           volatile int* abort_flag, volatile int* flag) {
+                                           volatile int* abort_flag, volatile int* flag,
+                                           int credit_ok, unsigned long long* trace) {
   const EngineParams::Xgpu& x = p.xg;
   // 1. This thread's bulk stores (TMA stores / reduce-adds) are complete in
   //    global memory and visible to generic-proxy loads of any SM.
@@ -620,18 +625,17 @@ __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, i
   ptx::fence_proxy_async_global();
   __threadfence();
   epi_bar_sync(threads);
+  if (trace && t == 0) trace[60] = ptx::globaltimer_ns();
   // 2. Grid-wide arrival in this rank's mailbox.  The count word carries the
-  //    epoch in its upper bits: a word left by another epoch (or by a launch
-  //    that gave up) counts as zero.
+  //    epoch in its upper bits: every CTA first raises it to at least this
+  //    epoch's tag (a word left by an earlier epoch, or by a launch that gave
+  //    up, drops to the tag), then adds one: two atomics per CTA and no retry
+  //    loop (a compare-and-swap loop serialises the grid's arrivals).
   unsigned long long* cnt = reinterpret_cast<unsigned long long*>(x.mbox[x.rank] + x.count_off);
   const unsigned long long tag = static_cast<unsigned long long>(x.epoch) << 20;
   if (t == 0) {
-    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(cnt), seen;
-    do {
-      seen = old;
-      const unsigned long long nv = (seen >> 20) == (tag >> 20) ? seen + 1 : tag + 1;
-      old = atomicCAS(cnt, seen, nv);
-    } while (old != seen);
+    atomicMax(cnt, tag);
+    atomicAdd(cnt, 1ull);
     const unsigned long long want = tag + gridDim.x;
     const uint64_t t0 = ptx::globaltimer_ns();
     int ok = 1;
@@ -643,7 +647,8 @@ __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, i
       __nanosleep(64);
     }
     if (!ok && !*abort_flag) record_error(p.err, abort_flag, kErrPeerGrid);
-    *flag = ok && !*abort_flag;
+    *flag = ok && !*abort_flag && (x.rank == x.root || credit_ok);
+    if (trace) trace[61] = ptx::globaltimer_ns();
   }
   epi_bar_sync(threads);
   if (!*flag) return;
@@ -656,18 +661,6 @@ __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, i
     const long long i0 = c * kPeerChunk;
     const long long i1 = i0 + kPeerChunk < x.elems ? i0 + kPeerChunk : x.elems;
     if (!is_root) {
-      // The slot this epoch writes was last read by the root two epochs ago.
-      if (t == 0) {
-        const uint64_t* consumed =
-            reinterpret_cast<const uint64_t*>(x.mbox[x.rank] + x.consumed_off) + c;
-        const long long need = x.epoch - 2;
-        const int ok = need <= 0 || peer_wait_at_least(consumed, static_cast<uint64_t>(need),
-                                                       p.wait_limit_ns);
-        if (!ok) record_error(p.err, abort_flag, kErrPeerCredit);
-        *flag = ok;
-      }
-      epi_bar_sync(threads);
-      if (!*flag) return;
       float* dst = reinterpret_cast<float*>(rootb + x.landing_off +
                                             (slot * x.world + x.rank) * x.slot_stride);
       for (long long i = i0 + 4ll * t; i < i1; i += 4ll * threads) {
@@ -734,6 +727,7 @@ __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, i
       }
     }
   }
+  if (trace && t == 0) trace[62] = ptx::globaltimer_ns();
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, bool X3, bool XF, bool PAIR, int EPIG,
@@ -1158,6 +1152,20 @@ __global__ void __launch_bounds__(
     const uint32_t tmem_empty_leader =
         PAIR ? ptx::mapa_shared(ptx::smem_addr(tmem_empty), 0) : 0u;
     uint32_t tl = 0, seq = 0;
+    if (p.xg.world > 1 && p.xg.rank != p.xg.root && ew == 0 && lane == 0) {
+      // Fused cross-GPU step, non-root: the landing slots this epoch writes
+      // were last read by the root two epochs ago; checked now, while the
+      // mainloop runs, so that the exchange itself waits on nothing local.
+      const EngineParams::Xgpu& x = p.xg;
+      int ok = 1;
+      for (long long c = blockIdx.x; ok && x.epoch > 2 && c < x.nchunk; c += gridDim.x) {
+        const uint64_t* consumed =
+            reinterpret_cast<const uint64_t*>(x.mbox[x.rank] + x.consumed_off) + c;
+        ok = peer_wait_at_least(consumed, static_cast<uint64_t>(x.epoch - 2), p.wait_limit_ns);
+      }
+      if (!ok) record_error(p.err, abort_flag, kErrPeerCredit);
+      *reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 12) = ok;
+    }
     // Zero this warp's chunks of a tile region (TMA zero boxes), wait until
     // the stores are complete, then stamp `flag` with the launch's epoch.
     auto zero_and_flag = [&](int row0, int n0, int b, unsigned* flag) {
@@ -1373,7 +1381,8 @@ __global__ void __launch_bounds__(
     if (p.xg.world > 1) {
       // Fused cross-GPU step (every CTA takes part, also one without units).
       xgpu_exchange(p, Cfg::kEpiWarps * 32, ew * 32 + lane, abort_flag,
-                    reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 8));
+                    reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 8),
+                    *reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 12), trace);
     } else if (lane == 0) {
       ptx::bulk_wait_read<0>();   // staging boxes read before the CTA exits
     }
