@@ -1404,7 +1404,6 @@ extern "C" int b2g_gemm_splitk_peer(const b2g_gemm_desc* d, void* const* mailbox
   x.epoch = epoch;
   x.elems = elems;
   x.nchunk = lay.nchunk;
-  x.ready_off = lay.ready_off;
   x.consumed_off = lay.consumed_off;
   x.count_off = lay.count_off;
   x.landing_off = lay.landing_off;

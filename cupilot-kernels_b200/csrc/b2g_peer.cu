@@ -8,15 +8,16 @@
 // over NVLink by the two kernels below, through peer memory:
 //
 //   non-root rank r: peer_push_kernel copies its partial, chunk by chunk,
-//     into landing slot [epoch % 2][r] of the root's mailbox with plain
-//     16-byte stores through the peer mapping, then stamps the chunk's
-//     ready flag ready[c][r] = epoch in the root's mailbox (release, system
-//     scope).  Before writing a chunk it waits until the root has consumed
-//     the same slot two epochs ago (consumed[c] in its own mailbox).
-//   root: peer_reduce_kernel waits for ready[c][r] >= epoch from every other
-//     rank, adds the landed chunks to its own partial (already in C, in rank
-//     order, so the sum is deterministic), and stamps consumed[c] = epoch in
-//     every other rank's mailbox.
+//     into landing slot [epoch % 2][r] of the root's mailbox through the
+//     peer mapping, each value as an 8-byte word {value, epoch} written by
+//     16-byte stores (no ready flag, no release fence).  Before writing a
+//     chunk it waits until the root has consumed the same slot two epochs
+//     ago (consumed[c] in its own mailbox).
+//   root: peer_reduce_kernel waits until every landed word of its chunk
+//     carries this epoch (polled while its own GEMM may still run), adds the
+//     values to its own partial (already in C, in rank order, so the sum is
+//     deterministic), and, once the previous epoch's kernels have finished,
+//     stamps consumed[c] = epoch - 1 in every other rank's mailbox.
 //
 // Every wait is bounded (B2G_WAIT_LIMIT_MS): a wait that gives up records a
 // code in the device error word and the CTA returns; nothing traps.  Only
@@ -88,22 +89,15 @@ __global__ void __launch_bounds__(kThreads) peer_push_kernel(const float* __rest
     if (threadIdx.x == 0 && err) atomicCAS(err, 0, kErrPeerCredit);
     return;
   }
-  float* dst = reinterpret_cast<float*>(rootb + lay.landing_off +
-                                        ((epoch & 1) * world + rank) * lay.slot_stride);
+  // Each value lands with the epoch in its flag half: no ready flag, no fence.
+  uint64_t* dst = reinterpret_cast<uint64_t*>(rootb + lay.landing_off +
+                                              ((epoch & 1) * world + rank) * lay.slot_stride);
+  const uint32_t flag = static_cast<uint32_t>(epoch);
   const int64_t i = c * kChunk + static_cast<int64_t>(threadIdx.x) * 4;
   if (i + 4 <= elems) {
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(partial + i));
-    *reinterpret_cast<float4*>(dst + i) = v;
+    b2g::peer_ll_put4(dst + i, __ldcg(reinterpret_cast<const float4*>(partial + i)), flag);
   } else {
-    for (int64_t j = i; j < elems; ++j) dst[j] = __ldcg(partial + j);
-  }
-  // The CTA barrier orders every thread's peer stores before thread 0's
-  // release store (cumulative at system scope): one fence per chunk, not
-  // one per thread.
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint64_t* ready = reinterpret_cast<uint64_t*>(rootb + lay.ready_off) + c * world + rank;
-    st_release_sys(ready, static_cast<uint64_t>(epoch));
+    for (int64_t j = i; j < elems; ++j) b2g::peer_ll_put1(dst + j, __ldcg(partial + j), flag);
   }
 }
 
@@ -121,32 +115,36 @@ __global__ void __launch_bounds__(kThreads) peer_reduce_kernel(float* __restrict
   if (threadIdx.x == 0) abort_flag = 0;
   __syncthreads();
   const int t = threadIdx.x;
-  // The other ranks' chunks (polled while this rank's GEMM may still run).
-  if (t < world && t != root) {
-    const uint64_t* ready = reinterpret_cast<const uint64_t*>(mine + lay.ready_off) + c * world + t;
-    if (!wait_at_least(ready, static_cast<uint64_t>(epoch), limit_ns)) {
-      atomicExch(&abort_flag, 1);
-      if (err) atomicCAS(err, 0, kErrPeerReady);
-    }
-  }
-  // out holds this rank's own partial, written by the preceding GEMM.
-  b2g::ptx::griddep_wait();
-  __syncthreads();
-  if (abort_flag) return;
-  const float* slot = reinterpret_cast<const float*>(mine + lay.landing_off +
-                                                     (epoch & 1) * world * lay.slot_stride);
-  const int64_t stride = lay.slot_stride / 4;
+  const uint32_t flag = static_cast<uint32_t>(epoch);
+  const uint64_t* slot = reinterpret_cast<const uint64_t*>(mine + lay.landing_off +
+                                                           (epoch & 1) * world * lay.slot_stride);
+  const int64_t stride = lay.slot_stride / 8;
   const int64_t i = c * kChunk + static_cast<int64_t>(t) * 4;
+  // The other ranks' values do not depend on this rank's GEMM: they are
+  // awaited and read while the GEMM may still run (programmatic launch).
+  float4 v[kMaxRanks];
+  bool ok = true;
   if (i + 4 <= elems) {
-    float4 acc = *reinterpret_cast<const float4*>(out + i);
-    // Every rank's landed chunk is loaded before any is added (the loads
-    // overlap), then summed in rank order.  L2 loads: the landed data was
-    // written by another GPU since this SM may last have cached the slot.
-    float4 v[kMaxRanks];
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r)
-      if (r < world && r != root)
-        v[r] = __ldcg(reinterpret_cast<const float4*>(slot + r * stride + i));
+      if (r < world && r != root && ok) ok = b2g::peer_ll_get4(slot + r * stride + i, flag,
+                                                              limit_ns, &v[r]);
+  }
+  if (!ok) {
+    atomicExch(&abort_flag, 1);
+    if (err) atomicCAS(err, 0, kErrPeerReady);
+  }
+  // out holds this rank's own partial, written by the preceding GEMM; the
+  // previous epoch's reduce has finished, so its slots are free again.
+  b2g::ptx::griddep_wait();
+  if (t < world && t != root && epoch > 1) {
+    uint64_t* consumed = reinterpret_cast<uint64_t*>(args.mbox[t] + lay.consumed_off) + c;
+    st_release_sys(consumed, static_cast<uint64_t>(epoch - 1));
+  }
+  __syncthreads();
+  if (abort_flag) return;
+  if (i + 4 <= elems) {
+    float4 acc = *reinterpret_cast<const float4*>(out + i);
 #pragma unroll
     for (int r = 0; r < kMaxRanks; ++r)
       if (r < world && r != root) {
@@ -159,15 +157,16 @@ __global__ void __launch_bounds__(kThreads) peer_reduce_kernel(float* __restrict
   } else {
     for (int64_t j = i; j < elems; ++j) {
       float acc = out[j];
-      for (int r = 0; r < world; ++r)
-        if (r != root) acc += __ldcg(slot + r * stride + j);
+      for (int r = 0; r < world; ++r) {
+        float x = 0.f;
+        if (r != root && !b2g::peer_ll_get1(slot + r * stride + j, flag, limit_ns, &x)) {
+          if (err) atomicCAS(err, 0, kErrPeerReady);
+          return;
+        }
+        if (r != root) acc += x;
+      }
       out[j] = acc;
     }
-  }
-  __syncthreads();   // every thread's reads of the slot are done
-  if (t < world && t != root) {
-    uint64_t* consumed = reinterpret_cast<uint64_t*>(args.mbox[t] + lay.consumed_off) + c;
-    st_release_sys(consumed, static_cast<uint64_t>(epoch));
   }
 }
 
@@ -186,9 +185,10 @@ extern "C" int b2g_peer_mailbox_create(int64_t elems, int world, void** mailbox,
   const Layout l = layout(elems, world);
   void* p = nullptr;
   if (cudaMalloc(&p, l.total) != cudaSuccess) return B2G_ERR_LAUNCH;
-  // Flags start at 0 (no epoch yet); landing slots need no initial value.
+  // Everything starts at 0: flags have no epoch yet, and no landing word
+  // carries an epoch's flag before a rank writes it.
   cudaIpcMemHandle_t h;
-  if (cudaMemset(p, 0, l.flag_bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+  if (cudaMemset(p, 0, l.total) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
     cudaFree(p);
     return B2G_ERR_LAUNCH;
   }

@@ -116,16 +116,16 @@ struct EngineParams {
   // ranks' partials on the root inside the same kernel, over the mailboxes
   // of peer_protocol.cuh: once every CTA's stores are complete (a grid-wide
   // count in this rank's mailbox), the epilogue warps of CTA i take protocol
-  // chunks i, i + grid, ...: a non-root rank copies them into its landing
-  // slot in the root's mailbox and stamps ready; the root waits for every
-  // rank's ready, adds the landed chunks to its own in rank order and stamps
-  // consumed.  Same flags, slots and order of additions as the stand-alone
+  // chunks i, i + grid, ...: a non-root rank writes them into its landing
+  // slot in the root's mailbox as {value, epoch} words; the root waits until
+  // every landed word carries the epoch and adds them to its own in rank
+  // order.  Same flags, slots and order of additions as the stand-alone
   // push / reduce kernels, so the two paths give identical sums.  Only plain
   // loads and stores touch peer memory.
   struct Xgpu {
     unsigned char* mbox[kPeerMaxRanks];   // every rank's mailbox as mapped here
     long long epoch, elems;
-    long long nchunk, ready_off, consumed_off, count_off, landing_off, slot_stride;
+    long long nchunk, consumed_off, count_off, landing_off, slot_stride;
     int world, rank, root;
   } xg;
 };
@@ -612,30 +612,56 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
 // epilogue threads of every CTA after their last store; t = thread index
 // among them, flag = a shared-memory word for broadcasting.
 // credit_ok: the non-root's slot credits, checked at the epilogue's start.
-// trace (tuning aid): words 60 stores complete, 61 grid arrival seen,
-// 62 exchange done (thread 0).
+// trace (tuning aid, thread 0): words 60 stores complete, 58 first landed
+// group read (root), 61 grid arrival seen, 63 landed values in registers,
+// 62 exchange done.
 __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, int t,
                                            volatile int* abort_flag, volatile int* flag,
                                            int credit_ok, unsigned long long* trace) {
   const EngineParams::Xgpu& x = p.xg;
   // 1. This thread's bulk stores (TMA stores / reduce-adds) are complete in
   //    global memory and visible to generic-proxy loads of any SM.
-  if ((t & 31) == 0) ptx::bulk_wait_all();
-  __syncwarp();
-  ptx::fence_proxy_async_global();
-  __threadfence();
+  if ((t & 31) == 0) {
+    ptx::bulk_wait_all();
+    ptx::fence_proxy_async_global();
+  }
   epi_bar_sync(threads);
   if (trace && t == 0) trace[60] = ptx::globaltimer_ns();
-  // 2. Grid-wide arrival in this rank's mailbox.  The count word carries the
-  //    epoch in its upper bits: every CTA first raises it to at least this
-  //    epoch's tag (a word left by an earlier epoch, or by a launch that gave
-  //    up, drops to the tag), then adds one: two atomics per CTA and no retry
-  //    loop (a compare-and-swap loop serialises the grid's arrivals).
+  // 2. Grid-wide arrival in this rank's mailbox (the wait for the others
+  //    comes below).  The count word carries the epoch in its upper bits:
+  //    every CTA first raises it to at least this epoch's tag (a word left
+  //    by an earlier epoch, or by a launch that gave up, drops to the tag),
+  //    then adds one: two atomics per CTA and no retry loop (a
+  //    compare-and-swap loop serialises the grid's arrivals).
   unsigned long long* cnt = reinterpret_cast<unsigned long long*>(x.mbox[x.rank] + x.count_off);
   const unsigned long long tag = static_cast<unsigned long long>(x.epoch) << 20;
   if (t == 0) {
+    __threadfence();   // release: the CTA's stores (ordered by the barrier) before the count
     atomicMax(cnt, tag);
     atomicAdd(cnt, 1ull);
+  }
+  // Root: the other ranks' values do not depend on this rank's other CTAs,
+  // so this thread's first group is awaited and read now, while the grid
+  // completes (its first access to the landing slot is the slow one).
+  const bool is_root = x.rank == x.root;
+  const uint32_t lflag = static_cast<uint32_t>(x.epoch);
+  const uint64_t* land_slot = reinterpret_cast<const uint64_t*>(
+      x.mbox[x.root] + x.landing_off + (x.epoch & 1) * x.world * x.slot_stride);
+  const long long stride = x.slot_stride / 8;   // words per (slot, rank) region
+  const long long i_pre = static_cast<long long>(blockIdx.x) * kPeerChunk + 4ll * t;
+  const bool have_pre = is_root && blockIdx.x < x.nchunk && 4ll * t < kPeerChunk &&
+                        i_pre + 4 <= x.elems;
+  float4 pre[kPeerMaxRanks];
+  bool pre_ok = true;
+  if (have_pre) {
+#pragma unroll
+    for (int r = 0; r < kPeerMaxRanks; ++r)
+      if (r < x.world && r != x.root && pre_ok)
+        pre_ok = peer_ll_get4(land_slot + r * stride + i_pre, lflag, p.wait_limit_ns, &pre[r]);
+  }
+  if (trace && t == 0) trace[58] = ptx::globaltimer_ns();
+  // 3. Wait until every CTA of the grid has arrived.
+  if (t == 0) {
     const unsigned long long want = tag + gridDim.x;
     const uint64_t t0 = ptx::globaltimer_ns();
     int ok = 1;
@@ -650,80 +676,69 @@ __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, i
     *flag = ok && !*abort_flag && (x.rank == x.root || credit_ok);
     if (trace) trace[61] = ptx::globaltimer_ns();
   }
+  // Thread 0's acquire of the count and the barrier order every thread's
+  // loads below after the other CTAs' stores.
   epi_bar_sync(threads);
   if (!*flag) return;
-  __threadfence();
-  const bool is_root = x.rank == x.root;
-  const long long slot = x.epoch & 1;
-  const float* own = p.C;
-  unsigned char* rootb = x.mbox[x.root];
+  float* out = p.C;
   for (long long c = blockIdx.x; c < x.nchunk; c += gridDim.x) {
     const long long i0 = c * kPeerChunk;
     const long long i1 = i0 + kPeerChunk < x.elems ? i0 + kPeerChunk : x.elems;
     if (!is_root) {
-      float* dst = reinterpret_cast<float*>(rootb + x.landing_off +
-                                            (slot * x.world + x.rank) * x.slot_stride);
+      // Each value lands with the epoch in its flag half: no ready flag and
+      // no fence on this path.
+      uint64_t* dst = const_cast<uint64_t*>(land_slot) + x.rank * stride;
       for (long long i = i0 + 4ll * t; i < i1; i += 4ll * threads) {
         if (i + 4 <= i1) {
-          *reinterpret_cast<float4*>(dst + i) = __ldcg(reinterpret_cast<const float4*>(own + i));
+          peer_ll_put4(dst + i, __ldcg(reinterpret_cast<const float4*>(out + i)), lflag);
         } else {
-          for (long long j = i; j < i1; ++j) dst[j] = __ldcg(own + j);
+          for (long long j = i; j < i1; ++j) peer_ll_put1(dst + j, __ldcg(out + j), lflag);
         }
-      }
-      // The barrier orders every thread's peer stores before thread 0's
-      // release store (cumulative at system scope).
-      epi_bar_sync(threads);
-      if (t == 0) {
-        uint64_t* ready = reinterpret_cast<uint64_t*>(rootb + x.ready_off) + c * x.world + x.rank;
-        peer_st_release_sys(ready, static_cast<uint64_t>(x.epoch));
       }
     } else {
-      if (t == 0) *flag = 1;
-      epi_bar_sync(threads);
-      if (t < x.world && t != x.root) {
-        const uint64_t* ready = reinterpret_cast<const uint64_t*>(rootb + x.ready_off) +
-                                c * x.world + t;
-        if (!peer_wait_at_least(ready, static_cast<uint64_t>(x.epoch), p.wait_limit_ns)) {
-          *flag = 0;
-          record_error(p.err, abort_flag, kErrPeerReady);
-        }
-      }
-      epi_bar_sync(threads);
-      if (!*flag) return;
-      const float* land = reinterpret_cast<const float*>(rootb + x.landing_off +
-                                                         slot * x.world * x.slot_stride);
-      const long long stride = x.slot_stride / 4;
-      float* out = p.C;
       for (long long i = i0 + 4ll * t; i < i1; i += 4ll * threads) {
+        bool ok = true;
         if (i + 4 <= i1) {
-          float4 acc = __ldcg(reinterpret_cast<const float4*>(out + i));
           float4 v[kPeerMaxRanks];
+          if (have_pre && i == i_pre) {
+            ok = pre_ok;
 #pragma unroll
-          for (int r = 0; r < kPeerMaxRanks; ++r)
-            if (r < x.world && r != x.root)
-              v[r] = __ldcg(reinterpret_cast<const float4*>(land + r * stride + i));
+            for (int r = 0; r < kPeerMaxRanks; ++r) v[r] = pre[r];
+          } else {
 #pragma unroll
-          for (int r = 0; r < kPeerMaxRanks; ++r)
-            if (r < x.world && r != x.root) {
-              acc.x += v[r].x;
-              acc.y += v[r].y;
-              acc.z += v[r].z;
-              acc.w += v[r].w;
-            }
-          *reinterpret_cast<float4*>(out + i) = acc;
+            for (int r = 0; r < kPeerMaxRanks; ++r)
+              if (r < x.world && r != x.root && ok)
+                ok = peer_ll_get4(land_slot + r * stride + i, lflag, p.wait_limit_ns, &v[r]);
+          }
+          if (trace && t == 0) trace[63] = ptx::globaltimer_ns();
+          if (ok) {
+            float4 acc = __ldcg(reinterpret_cast<const float4*>(out + i));
+#pragma unroll
+            for (int r = 0; r < kPeerMaxRanks; ++r)
+              if (r < x.world && r != x.root) {
+                acc.x += v[r].x;
+                acc.y += v[r].y;
+                acc.z += v[r].z;
+                acc.w += v[r].w;
+              }
+            *reinterpret_cast<float4*>(out + i) = acc;
+          }
         } else {
-          for (long long j = i; j < i1; ++j) {
+          for (long long j = i; j < i1 && ok; ++j) {
             float acc = __ldcg(out + j);
-            for (int r = 0; r < x.world; ++r)
-              if (r != x.root) acc += __ldcg(land + r * stride + j);
-            out[j] = acc;
+            for (int r = 0; r < x.world && ok; ++r) {
+              float v = 0.f;
+              if (r != x.root) ok = peer_ll_get1(land_slot + r * stride + j, lflag,
+                                                 p.wait_limit_ns, &v);
+              acc += v;
+            }
+            if (ok) out[j] = acc;
           }
         }
-      }
-      epi_bar_sync(threads);   // every thread's reads of the slot are done
-      if (t < x.world && t != x.root) {
-        uint64_t* consumed = reinterpret_cast<uint64_t*>(x.mbox[t] + x.consumed_off) + c;
-        peer_st_release_sys(consumed, static_cast<uint64_t>(x.epoch));
+        if (!ok) {
+          record_error(p.err, abort_flag, kErrPeerReady);
+          break;
+        }
       }
     }
   }
@@ -1152,6 +1167,17 @@ __global__ void __launch_bounds__(
     const uint32_t tmem_empty_leader =
         PAIR ? ptx::mapa_shared(ptx::smem_addr(tmem_empty), 0) : 0u;
     uint32_t tl = 0, seq = 0;
+    if (p.xg.world > 1 && p.xg.rank == p.xg.root && ew == 0 && lane == 0 && p.xg.epoch > 1) {
+      // Fused cross-GPU step, root: the previous epoch's kernels have
+      // finished (this one is past its grid-dependency wait), so the other
+      // ranks may reuse the landing slots of epoch - 1.
+      const EngineParams::Xgpu& x = p.xg;
+      for (long long c = blockIdx.x; c < x.nchunk; c += gridDim.x)
+        for (int r = 0; r < x.world; ++r)
+          if (r != x.root)
+            peer_st_release_sys(reinterpret_cast<uint64_t*>(x.mbox[r] + x.consumed_off) + c,
+                                static_cast<uint64_t>(x.epoch - 1));
+    }
     if (p.xg.world > 1 && p.xg.rank != p.xg.root && ew == 0 && lane == 0) {
       // Fused cross-GPU step, non-root: the landing slots this epoch writes
       // were last read by the root two epochs ago; checked now, while the
