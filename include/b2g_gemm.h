@@ -241,10 +241,12 @@ B2G_API int b2g_sdpa(const void* q, const void* k, const void* v, void* out, int
  * Here each rank multiplies its K slice with b2g_gemm and then calls
  * b2g_splitk_peer_reduce on the same stream: a non-root rank copies its
  * partial into a landing slot of the root's mailbox through the peer
- * mapping (plain stores over NVLink) and stamps a per-chunk flag; the root
- * waits (bounded) for every chunk from every rank and adds them, in rank
- * order, into `out`, which already holds its own partial.  C = sum of the
- * partials lands on the root only.
+ * mapping (plain stores over NVLink, each value carrying the epoch); the
+ * root waits (bounded) until every value of every rank has landed and adds
+ * them, in rank order, into `out`, which already holds its own partial.
+ * C = sum of the partials lands on the root only.  One stream per mailbox
+ * set: the root frees the previous epoch's landing slots when its next
+ * epoch's kernel starts.
  *
  * Mailboxes: each rank creates one (b2g_peer_mailbox_create, device memory
  * of b2g_peer_mailbox_bytes(elems, world)), shares its IPC handle with the
@@ -253,7 +255,7 @@ B2G_API int b2g_sdpa(const void* q, const void* k, const void* v, void* out, int
  * own pointer for r == rank).  All ranks call with the same epoch, 1, 2, 3,
  * ... per mailbox set; a rank may run at most one epoch ahead of the root
  * (it waits, bounded, for the root to free the landing slot).  A wait that
- * gives up records 0x201 (slot credit) or 0x202 (chunk not ready) in the
+ * gives up records 0x201 (slot credit) or 0x202 (values not landed) in the
  * device error word (b2g_read_device_error) and the call's output is
  * incomplete.  partial / out: elems fp32, 16-byte aligned.
  */
