@@ -14,8 +14,8 @@
 //     chunk it waits until the root has consumed the same slot two epochs
 //     ago (consumed[c] in its own mailbox).
 //   root: peer_reduce_kernel waits until every landed word of its chunk
-//     carries this epoch (polled while its own GEMM may still run), adds the
-//     values to its own partial (already in C, in rank order, so the sum is
+//     carries this epoch (polled while its own GEMM may still run), sums
+//     them in rank order and adds the sum to its own partial (already in C;
 //     deterministic), and, once the previous epoch's kernels have finished,
 //     stamps consumed[c] = epoch - 1 in every other rank's mailbox.
 //
@@ -121,15 +121,10 @@ __global__ void __launch_bounds__(kThreads) peer_reduce_kernel(float* __restrict
   const int64_t stride = lay.slot_stride / 8;
   const int64_t i = c * kChunk + static_cast<int64_t>(t) * 4;
   // The other ranks' values do not depend on this rank's GEMM: they are
-  // awaited and read while the GEMM may still run (programmatic launch).
-  float4 v[kMaxRanks];
+  // awaited, read and summed (rank order) while the GEMM may still run.
+  float4 lsum = make_float4(0.f, 0.f, 0.f, 0.f);
   bool ok = true;
-  if (i + 4 <= elems) {
-#pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r)
-      if (r < world && r != root && ok) ok = b2g::peer_ll_get4(slot + r * stride + i, flag,
-                                                              limit_ns, &v[r]);
-  }
+  if (i + 4 <= elems) ok = b2g::peer_ll_sum4(slot, stride, world, root, i, flag, limit_ns, &lsum);
   if (!ok) {
     atomicExch(&abort_flag, 1);
     if (err) atomicCAS(err, 0, kErrPeerReady);
@@ -143,29 +138,27 @@ __global__ void __launch_bounds__(kThreads) peer_reduce_kernel(float* __restrict
   }
   __syncthreads();
   if (abort_flag) return;
+  // out + (sum of the other ranks' partials): the same order as the fused
+  // kernel's, so the two paths give identical sums.
   if (i + 4 <= elems) {
     float4 acc = *reinterpret_cast<const float4*>(out + i);
-#pragma unroll
-    for (int r = 0; r < kMaxRanks; ++r)
-      if (r < world && r != root) {
-        acc.x += v[r].x;
-        acc.y += v[r].y;
-        acc.z += v[r].z;
-        acc.w += v[r].w;
-      }
+    acc.x += lsum.x;
+    acc.y += lsum.y;
+    acc.z += lsum.z;
+    acc.w += lsum.w;
     *reinterpret_cast<float4*>(out + i) = acc;
   } else {
     for (int64_t j = i; j < elems; ++j) {
-      float acc = out[j];
+      float s = 0.f;
       for (int r = 0; r < world; ++r) {
         float x = 0.f;
         if (r != root && !b2g::peer_ll_get1(slot + r * stride + j, flag, limit_ns, &x)) {
           if (err) atomicCAS(err, 0, kErrPeerReady);
           return;
         }
-        if (r != root) acc += x;
+        s += x;
       }
-      out[j] = acc;
+      out[j] += s;
     }
   }
 }

@@ -615,10 +615,14 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
 // trace (tuning aid, thread 0): words 60 stores complete, 58 first landed
 // group read (root), 61 grid arrival seen, 63 landed values in registers,
 // 62 exchange done.
-__device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, int t,
+// Not inlined, and given a copy of the exchange's parameters rather than the
+// kernel's: the mainloop's register allocation and parameter accesses stay
+// as they are without the exchange.
+__device__ __noinline__ void xgpu_exchange(const EngineParams::Xgpu* xp, float* out_c,
+                                           long long wait_limit_ns, int* err, int threads, int t,
                                            volatile int* abort_flag, volatile int* flag,
                                            int credit_ok, unsigned long long* trace) {
-  const EngineParams::Xgpu& x = p.xg;
+  const EngineParams::Xgpu& x = *xp;
   // 1. This thread's bulk stores (TMA stores / reduce-adds) are complete in
   //    global memory and visible to generic-proxy loads of any SM.
   if ((t & 31) == 0) {
@@ -651,14 +655,10 @@ __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, i
   const long long i_pre = static_cast<long long>(blockIdx.x) * kPeerChunk + 4ll * t;
   const bool have_pre = is_root && blockIdx.x < x.nchunk && 4ll * t < kPeerChunk &&
                         i_pre + 4 <= x.elems;
-  float4 pre[kPeerMaxRanks];
+  float4 pre = make_float4(0.f, 0.f, 0.f, 0.f);   // landed values, summed in rank order
   bool pre_ok = true;
-  if (have_pre) {
-#pragma unroll
-    for (int r = 0; r < kPeerMaxRanks; ++r)
-      if (r < x.world && r != x.root && pre_ok)
-        pre_ok = peer_ll_get4(land_slot + r * stride + i_pre, lflag, p.wait_limit_ns, &pre[r]);
-  }
+  if (have_pre) pre_ok = peer_ll_sum4(land_slot, stride, x.world, x.root, i_pre, lflag,
+                                      wait_limit_ns, &pre);
   if (trace && t == 0) trace[58] = ptx::globaltimer_ns();
   // 3. Wait until every CTA of the grid has arrived.
   if (t == 0) {
@@ -666,13 +666,13 @@ __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, i
     const uint64_t t0 = ptx::globaltimer_ns();
     int ok = 1;
     while (ld_acquire_gpu_u64(cnt) != want) {
-      if (*abort_flag || ptx::globaltimer_ns() - t0 > static_cast<uint64_t>(p.wait_limit_ns)) {
+      if (*abort_flag || ptx::globaltimer_ns() - t0 > static_cast<uint64_t>(wait_limit_ns)) {
         ok = 0;
         break;
       }
       __nanosleep(64);
     }
-    if (!ok && !*abort_flag) record_error(p.err, abort_flag, kErrPeerGrid);
+    if (!ok && !*abort_flag) record_error(err, abort_flag, kErrPeerGrid);
     *flag = ok && !*abort_flag && (x.rank == x.root || credit_ok);
     if (trace) trace[61] = ptx::globaltimer_ns();
   }
@@ -680,7 +680,7 @@ __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, i
   // loads below after the other CTAs' stores.
   epi_bar_sync(threads);
   if (!*flag) return;
-  float* out = p.C;
+  float* out = out_c;
   for (long long c = blockIdx.x; c < x.nchunk; c += gridDim.x) {
     const long long i0 = c * kPeerChunk;
     const long long i1 = i0 + kPeerChunk < x.elems ? i0 + kPeerChunk : x.elems;
@@ -699,44 +699,34 @@ __device__ __noinline__ void xgpu_exchange(const EngineParams& p, int threads, i
       for (long long i = i0 + 4ll * t; i < i1; i += 4ll * threads) {
         bool ok = true;
         if (i + 4 <= i1) {
-          float4 v[kPeerMaxRanks];
-          if (have_pre && i == i_pre) {
+          float4 lsum = pre;
+          if (!(have_pre && i == i_pre))
+            ok = peer_ll_sum4(land_slot, stride, x.world, x.root, i, lflag, wait_limit_ns, &lsum);
+          else
             ok = pre_ok;
-#pragma unroll
-            for (int r = 0; r < kPeerMaxRanks; ++r) v[r] = pre[r];
-          } else {
-#pragma unroll
-            for (int r = 0; r < kPeerMaxRanks; ++r)
-              if (r < x.world && r != x.root && ok)
-                ok = peer_ll_get4(land_slot + r * stride + i, lflag, p.wait_limit_ns, &v[r]);
-          }
           if (trace && t == 0) trace[63] = ptx::globaltimer_ns();
           if (ok) {
             float4 acc = __ldcg(reinterpret_cast<const float4*>(out + i));
-#pragma unroll
-            for (int r = 0; r < kPeerMaxRanks; ++r)
-              if (r < x.world && r != x.root) {
-                acc.x += v[r].x;
-                acc.y += v[r].y;
-                acc.z += v[r].z;
-                acc.w += v[r].w;
-              }
+            acc.x += lsum.x;
+            acc.y += lsum.y;
+            acc.z += lsum.z;
+            acc.w += lsum.w;
             *reinterpret_cast<float4*>(out + i) = acc;
           }
         } else {
           for (long long j = i; j < i1 && ok; ++j) {
-            float acc = __ldcg(out + j);
+            float lsum = 0.f;
             for (int r = 0; r < x.world && ok; ++r) {
               float v = 0.f;
               if (r != x.root) ok = peer_ll_get1(land_slot + r * stride + j, lflag,
-                                                 p.wait_limit_ns, &v);
-              acc += v;
+                                                 wait_limit_ns, &v);
+              lsum += v;
             }
-            if (ok) out[j] = acc;
+            if (ok) out[j] = __ldcg(out + j) + lsum;
           }
         }
         if (!ok) {
-          record_error(p.err, abort_flag, kErrPeerReady);
+          record_error(err, abort_flag, kErrPeerReady);
           break;
         }
       }
@@ -1406,7 +1396,9 @@ __global__ void __launch_bounds__(
     }
     if (p.xg.world > 1) {
       // Fused cross-GPU step (every CTA takes part, also one without units).
-      xgpu_exchange(p, Cfg::kEpiWarps * 32, ew * 32 + lane, abort_flag,
+      const EngineParams::Xgpu xg_copy = p.xg;
+      xgpu_exchange(&xg_copy, p.C, p.wait_limit_ns, p.err, Cfg::kEpiWarps * 32, ew * 32 + lane,
+                    abort_flag,
                     reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 8),
                     *reinterpret_cast<volatile int*>(smem + Cfg::kOffMisc + 12), trace);
     } else if (lane == 0) {

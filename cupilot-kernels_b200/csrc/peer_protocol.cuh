@@ -111,6 +111,24 @@ __device__ __forceinline__ bool peer_ll_get1(const uint64_t* word, uint32_t flag
   *out = __uint_as_float(a);
   return true;
 }
+// The landed values i .. i+3 of every rank but `root`, summed in rank order
+// (the root then adds the sum to its own partial: out + (p_a + p_b + ...)).
+__device__ __forceinline__ bool peer_ll_sum4(const uint64_t* slot, long long stride, int world,
+                                             int root, long long i, uint32_t flag,
+                                             long long limit_ns, float4* sum) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r = 0; r < world; ++r) {
+    if (r == root) continue;
+    float4 v;
+    if (!peer_ll_get4(slot + r * stride + i, flag, limit_ns, &v)) return false;
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  *sum = acc;
+  return true;
+}
 #endif
 
 }  // namespace b2g

@@ -242,8 +242,9 @@ B2G_API int b2g_sdpa(const void* q, const void* k, const void* v, void* out, int
  * b2g_splitk_peer_reduce on the same stream: a non-root rank copies its
  * partial into a landing slot of the root's mailbox through the peer
  * mapping (plain stores over NVLink, each value carrying the epoch); the
- * root waits (bounded) until every value of every rank has landed and adds
- * them, in rank order, into `out`, which already holds its own partial.
+ * root waits (bounded) until every value of every rank has landed, sums
+ * them in rank order and adds the sum to `out`, which already holds its
+ * own partial.
  * C = sum of the partials lands on the root only.  One stream per mailbox
  * set: the root frees the previous epoch's landing slots when its next
  * epoch's kernel starts.
@@ -277,7 +278,7 @@ B2G_API int b2g_splitk_peer_reduce(const float* partial, float* out, int64_t ele
  * M x N with ldc == n, 16-byte aligned) is computed into d->c, and once every
  * CTA's stores are complete the same kernel's epilogue warps move it over
  * NVLink: a non-root rank copies it chunk by chunk into its landing slot in
- * the root's mailbox; the root adds the landed chunks, in rank order, to its
+ * the root's mailbox; the root adds the landed chunks (summed in rank order) to its
  * own C.  The mailboxes, epochs and flags are those of
  * b2g_splitk_peer_reduce (mailboxes of b2g_peer_mailbox_bytes(m * n, world)),
  * and the sum is bit-identical to b2g_gemm followed by
