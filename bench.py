@@ -427,8 +427,9 @@ def main():
     ap.add_argument("--profile-case", default="",
                     help="run only this workload (name) for --steps calls, untimed: the "
                          "command an ncu capture of one config wraps")
-    ap.add_argument("--profile-impl", choices=["ours", "cublas"], default="ours",
-                    help="--profile-case: our operator or the same math through cuBLAS")
+    ap.add_argument("--profile-impl", choices=["ours", "cublas", "fused"], default="ours",
+                    help="--profile-case: our operator, the same math through cuBLAS, or (large_k) "
+                         "the one-kernel cross-GPU K split with two ranks emulated on one GPU")
     ap.add_argument("--set", action="append", default=[],
                     help="dim=value override of the --profile-case workload's shape")
     ap.add_argument("--no-e2e", action="store_true")
@@ -546,6 +547,26 @@ def profile_case(W, args):
     w = W[args.profile_case]
     over = {k: int(v) for k, v in (x.split("=") for x in args.set)}
     ins = device_inputs(w, **over)
+    if args.profile_impl == "fused":
+        # b2g_gemm_splitk_peer with two ranks emulated on this GPU, one after
+        # the other (rank 1, then the root), the device synchronised between
+        # them: no kernel waits for another that runs beside it.
+        capi = _pkg("capi")
+        nat = importlib.import_module(PKG).native()
+        A, B = ins[0], ins[1]
+        h = A.shape[1] // 2
+        halves = [(A[:, :h].contiguous(), B[:h].contiguous()), (A[:, h:].contiguous(), B[h:].contiguous())]
+        mb = [capi.peer_mailbox_create(A.shape[0] * B.shape[1], 2)[0] for _ in range(2)]
+        for epoch in range(1, args.warmup + args.steps + 1):
+            for rk in (1, 0):
+                nat.splitk_peer_matmul(*halves[rk], mb, rk, 0, epoch)
+                torch.cuda.synchronize()
+        for ptr in mb:
+            capi.peer_mailbox_destroy(ptr)
+        print(json.dumps({"profile_case": w.name, "impl": "fused", "shapes": dict(w.shapes, **over),
+                          "calls": 2 * (args.warmup + args.steps),
+                          "device_error": ops.read_device_error(torch.cuda.current_device())}))
+        return
     if args.profile_impl == "cublas":
         op = lambda *a: cublas_fn(w.name, *a)()
     else:
