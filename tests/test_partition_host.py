@@ -84,6 +84,27 @@ def _worker(rank, world, port, scenario, q):
                     red.reduce(part_t, None, root=0)
             red.close()
             q.put(("peer", rank, red.epoch, fake.calls, fake.closed, fake.destroyed))
+        elif scenario == "fused_orchestration":
+            fake = FakePeerBackend(rank)
+            red = p.peer_reducer(M * N, backend=fake)
+            k0, k1 = p.k_range(K)
+            part_t = torch.zeros(M, N)
+            outs = []
+            for step in range(4):            # epochs alternate: fused, two-kernel, ...
+                if step % 2 == 0:
+                    C = red.matmul(A[:, k0:k1], B[k0:k1], root=0)
+                    outs.append(float((C - A[:, k0:k1] @ B[k0:k1]).abs().max()))
+                else:
+                    red.reduce(None, part_t, root=0) if rank == 0 else \
+                        red.reduce(part_t, None, root=0)
+            try:
+                red.matmul(A[:, :3], B[:3, :5], root=0)
+                bad = "accepted"
+            except ValueError:
+                bad = "rejected"
+            red.close()
+            q.put(("fused", rank, red.epoch, fake.fused, [c[6] for c in fake.calls], max(outs),
+                   bad))
         elif scenario == "dead_peer":
             if rank == 1:
                 os._exit(3)          # leaves between steps, nothing in flight
@@ -124,6 +145,10 @@ class FakePeerBackend:
     def splitk_peer_reduce(self, partial, out, elems, mailboxes, rank, root, epoch, stream):
         self.calls.append((bool(partial), bool(out), elems, list(mailboxes), rank, root, epoch))
         return 0
+
+    def torch_gemm_splitk_peer(self, A, B, mailboxes, rank, root, epoch):
+        self.__dict__.setdefault("fused", []).append((list(mailboxes), rank, root, epoch))
+        return A @ B
 
 
 def _run(scenario, world=2, timeout=60):
@@ -187,3 +212,22 @@ def test_peer_reducer_exchanges_handles_and_counts_epochs():
             assert (partial, outp) == ((False, True) if rank == 0 else (True, False))
         assert closed == [t for i, t in enumerate(table) if i != rank]
         assert destroyed == [1000 + rank]
+
+
+def test_fused_split_k_shares_the_epoch_sequence_with_the_two_kernel_path():
+    """PeerReducer.matmul (the one-kernel K split, b2g_gemm_splitk_peer) on
+    gloo ranks with a stand-in binding: it passes this rank's slices, the
+    mailbox table, the rank and the root, and draws its epochs from the same
+    counter as reduce(), so the two paths alternate epoch by epoch (1, 3 fused;
+    2, 4 two-kernel); a product of another size than the mailbox's is
+    rejected."""
+    out, codes = _run("fused_orchestration")
+    assert codes == [0, 0]
+    res = {o[1]: o for o in out if o[0] == "fused"}
+    assert set(res) == {0, 1}
+    for rank, (_, _, epoch, fused, reduce_epochs, err, bad) in res.items():
+        table = [1000, 2001] if rank == 0 else [2000, 1001]
+        assert epoch == 4
+        assert [f[3] for f in fused] == [1, 3] and reduce_epochs == [2, 4]
+        assert all(f[0] == table and f[1] == rank and f[2] == 0 for f in fused)
+        assert err < 1e-12 and bad == "rejected"
